@@ -1,0 +1,29 @@
+// internal.h -- launchers shared between the kernel files and the C-ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/cvattn.h"
+
+namespace cvattn {
+
+// kv_append.cu
+cudaError_t launch_kv_append(cudaStream_t stream, const cvattn_tensor& cache, const float* src, int64_t src_nb1,
+                             int64_t src_nb2, const int32_t* pos, int64_t pos_stride, int n_new, int batch,
+                             int* status);
+cudaError_t launch_kv_dequant(cudaStream_t stream, const cvattn_tensor& cache, int n_rows, float* dst);
+
+// decode.cu
+int decode_chunk_positions(int k_type, int v_type, int n_kv_heads, int head_dim);
+size_t decode_workspace_bytes(int k_type, int v_type, int n_seq, int max_kv_len, int n_q_heads, int n_kv_heads, int head_dim);
+bool decode_supported(int k_type, int v_type, int head_dim, int n_q_heads, int n_kv_heads);
+cudaError_t launch_decode(cudaStream_t stream, const cvattn_decode_params& p, int* status);
+cudaError_t launch_combine(cudaStream_t stream, const float* partial_o, const float* partial_ml, int n_parts,
+                           int n_rows, int head_dim, float* out);
+
+// flash_tc.cu
+bool flash_supported(int k_type, int v_type, int head_dim, int n_q_heads, int n_kv_heads);
+cudaError_t launch_flash(cudaStream_t stream, const cvattn_flash_params& p, int* status);
+
+}  // namespace cvattn

@@ -1,0 +1,107 @@
+// kv_append.cu -- fused quantize-on-write of new K/V rows into a ggml-layout
+// cache tensor: the ggml_set_rows of cosyvoice_kv_cache::update_cache
+// (src/cosyvoice-kv-cache.cpp:315-316,321-322), plus the inverse
+// (dequantize rows to f32) used for slot export and tests.
+//
+// One warp handles one 32-element group of one row; blocks are bit-identical
+// to ggml's reference quantizers (see quantize_block_warp in common.cuh).
+// HBM-bound: reads 128 B of f32 per group, writes 18-128 B.
+#include "common.cuh"
+#include "internal.h"
+
+namespace cvattn {
+
+template <int T>
+__global__ void __launch_bounds__(256) kv_append_kernel(
+    uint8_t* __restrict__ cache, int64_t nb1, int64_t nb2, int64_t capacity, int groups_per_row,
+    const float* __restrict__ src, int64_t src_nb1, int64_t src_nb2,
+    const int32_t* __restrict__ pos, int64_t pos_stride, int n_new, int batch, int* status) {
+    const int lane = threadIdx.x & 31;
+    const int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t total = (int64_t)n_new * batch * groups_per_row;
+    if (w >= total) return;
+    const int g = (int)(w % groups_per_row);
+    const int64_t r = w / groups_per_row;
+    const int t = (int)(r % n_new);
+    const int b = (int)(r / n_new);
+    const int p = pos[t + (int64_t)b * pos_stride];
+    if (p < 0 || p >= capacity) {
+        if (lane == 0) record_status(status, kStatusBadPosition);
+        return;
+    }
+    const float x = *reinterpret_cast<const float*>(
+        reinterpret_cast<const uint8_t*>(src) + t * src_nb1 + b * src_nb2 + ((int64_t)g * 32 + lane) * 4);
+    uint8_t* dst = cache + b * nb2 + (int64_t)p * nb1 + (int64_t)g * group_bytes(T);
+    quantize_block_warp<T>(x, dst, lane);
+}
+
+template <int T>
+__global__ void __launch_bounds__(256) kv_dequant_kernel(
+    const uint8_t* __restrict__ cache, int64_t nb1, int64_t nb2, int groups_per_row, int n_rows, int batch,
+    float* __restrict__ dst) {
+    const int lane = threadIdx.x & 31;
+    const int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t total = (int64_t)n_rows * batch * groups_per_row;
+    if (w >= total) return;
+    const int g = (int)(w % groups_per_row);
+    const int64_t r = w / groups_per_row;
+    const int t = (int)(r % n_rows);
+    const int b = (int)(r / n_rows);
+    const uint8_t* grp = cache + b * nb2 + (int64_t)t * nb1 + (int64_t)g * group_bytes(T);
+    dst[(((int64_t)b * n_rows + t) * groups_per_row + g) * 32 + lane] = dequant_elem<T>(grp, lane);
+}
+
+cudaError_t launch_kv_append(cudaStream_t stream, const cvattn_tensor& c, const float* src, int64_t src_nb1,
+                             int64_t src_nb2, const int32_t* pos, int64_t pos_stride, int n_new, int batch,
+                             int* status) {
+    const int row_elems = c.n_heads * c.head_dim;
+    const int groups = row_elems / 32;
+    const int64_t warps = (int64_t)n_new * batch * groups;
+    if (warps == 0) return cudaSuccess;
+    const unsigned grid = (unsigned)((warps + 7) / 8);
+    uint8_t* base = static_cast<uint8_t*>(c.data);
+#define CVATTN_APPEND_CASE(T)                                                                              \
+    case T:                                                                                                \
+        kv_append_kernel<T><<<grid, 256, 0, stream>>>(base, c.nb1, c.nb2, c.ne1, groups, src, src_nb1,     \
+                                                      src_nb2, pos, pos_stride, n_new, batch, status);     \
+        break;
+    switch (c.type) {
+        CVATTN_APPEND_CASE(kF32)
+        CVATTN_APPEND_CASE(kF16)
+        CVATTN_APPEND_CASE(kQ4_0)
+        CVATTN_APPEND_CASE(kQ4_1)
+        CVATTN_APPEND_CASE(kQ5_0)
+        CVATTN_APPEND_CASE(kQ5_1)
+        CVATTN_APPEND_CASE(kQ8_0)
+    default: return cudaErrorInvalidValue;
+    }
+#undef CVATTN_APPEND_CASE
+    return cudaGetLastError();
+}
+
+cudaError_t launch_kv_dequant(cudaStream_t stream, const cvattn_tensor& c, int n_rows, float* dst) {
+    const int row_elems = c.n_heads * c.head_dim;
+    const int groups = row_elems / 32;
+    const int64_t warps = (int64_t)n_rows * c.ne2 * groups;
+    if (warps == 0) return cudaSuccess;
+    const unsigned grid = (unsigned)((warps + 7) / 8);
+    const uint8_t* base = static_cast<const uint8_t*>(c.data);
+#define CVATTN_DEQ_CASE(T)                                                                                  \
+    case T:                                                                                                 \
+        kv_dequant_kernel<T><<<grid, 256, 0, stream>>>(base, c.nb1, c.nb2, groups, n_rows, (int)c.ne2, dst); \
+        break;
+    switch (c.type) {
+        CVATTN_DEQ_CASE(kF32)
+        CVATTN_DEQ_CASE(kF16)
+        CVATTN_DEQ_CASE(kQ4_0)
+        CVATTN_DEQ_CASE(kQ4_1)
+        CVATTN_DEQ_CASE(kQ5_0)
+        CVATTN_DEQ_CASE(kQ5_1)
+        CVATTN_DEQ_CASE(kQ8_0)
+    default: return cudaErrorInvalidValue;
+    }
+#undef CVATTN_DEQ_CASE
+    return cudaGetLastError();
+}
+
+}  // namespace cvattn

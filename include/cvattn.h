@@ -1,0 +1,335 @@
+/*
+ * cvattn.h -- C ABI of the B200 attention engine for cosyvoice.cpp.
+ *
+ * The engine replaces the ggml_flash_attn_ext attention path of cosyvoice.cpp
+ * (KV append/quantize, Qwen2 decode and prefill attention, DiT attention with
+ * fixed / offloadable / uncached KV slots).  Every entry point is plain C:
+ * device pointers, sizes and ggml type ids; no C++ or torch types.
+ *
+ * Conventions
+ *   - KV memory follows ggml's cache tensor layout (src/cosyvoice-kv-cache.cpp:104-119):
+ *     a tensor of type T with ne = {n_heads*head_dim, ne1 positions, ne2 batch};
+ *     one row (one position) holds every KV head, block-quantized for the
+ *     32-element types; nb1 = bytes between positions, nb2 = between batch entries.
+ *   - Streams are passed as void* (a cudaStream_t / CUstream); 0 = legacy default.
+ *   - Calls are asynchronous on the stream and never abort the process: bad
+ *     arguments return a status; bad device-resident indices are skipped and
+ *     recorded in the context's status word (cvattn_context_sync_status).
+ *   - Type ids are ggml's: F32=0, F16=1, Q4_0=2, Q4_1=3, Q5_0=6, Q5_1=7, Q8_0=8.
+ *   - Each worker thread uses its own cvattn_context and stream
+ *     (src/cosyvoice-model.cpp:82-107 gives each worker its own backend).
+ */
+#ifndef CVATTN_H
+#define CVATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CVATTN_ABI_VERSION 1
+
+/* ------------------------------------------------------------------ status */
+
+typedef enum cvattn_status {
+    CVATTN_OK = 0,
+    CVATTN_ERR_INVALID_ARGUMENT = 1,
+    CVATTN_ERR_UNSUPPORTED = 2,   /* type pair / head shape the engine does not implement */
+    CVATTN_ERR_LENGTH = 3,        /* sequence longer than the cache (src/cosyvoice-llm.cpp:98-99,207) */
+    CVATTN_ERR_ALLOC = 4,
+    CVATTN_ERR_CUDA = 5,          /* a CUDA runtime call failed */
+    CVATTN_ERR_DEVICE = 6,        /* a kernel skipped work on a bad device-resident index */
+    CVATTN_ERR_NO_DEVICE = 7,
+    CVATTN_ERR_TIMEOUT = 8        /* a bounded in-kernel wait gave up */
+} cvattn_status;
+
+/* Human-readable status text. */
+const char* cvattn_status_string(cvattn_status s);
+
+/* Maps a status onto enum ggml_status (SUCCESS 0, FAILED -1, ALLOC_FAILED -2),
+ * the value cosyvoice_worker_context::status holds (src/cosyvoice-model.cpp:522-525). */
+int32_t cvattn_status_to_ggml(cvattn_status s);
+
+/* ABI version and struct sizes, so bindings can verify their mirrors.
+ * which: 0 cvattn_tensor, 1 cvattn_decode_params, 2 cvattn_flash_params,
+ *        3 cvattn_kv_cache_params, 4 cvattn_dit_step. */
+int32_t cvattn_abi_version(void);
+size_t cvattn_abi_sizeof(int32_t which);
+
+/* ------------------------------------------------------------------- types */
+
+enum {
+    CVATTN_TYPE_F32 = 0, CVATTN_TYPE_F16 = 1, CVATTN_TYPE_Q4_0 = 2, CVATTN_TYPE_Q4_1 = 3,
+    CVATTN_TYPE_Q5_0 = 6, CVATTN_TYPE_Q5_1 = 7, CVATTN_TYPE_Q8_0 = 8
+};
+
+/* A ggml KV tensor (or an uncached K/V activation in the same row layout). */
+typedef struct cvattn_tensor {
+    void*   data;      /* device address of position 0, batch 0 */
+    int32_t type;      /* ggml type id */
+    int32_t n_heads;   /* heads packed in one row */
+    int32_t head_dim;  /* elements per head */
+    int32_t reserved;  /* 0 */
+    int64_t ne1;       /* positions (capacity) */
+    int64_t ne2;       /* batch entries */
+    int64_t nb1;       /* bytes between positions */
+    int64_t nb2;       /* bytes between batch entries */
+} cvattn_tensor;
+
+/* ggml_row_size(type, n): bytes of n elements; 0 for an unknown type or a
+ * count that is not a multiple of the block size. */
+size_t cvattn_row_size(int32_t type, int64_t n);
+
+/* ---------------------------------------------------- capability and types */
+
+/* Replaces the ggml_backend_supports_op probes on set_rows + flash_attn_ext
+ * (src/cosyvoice-loader.cpp:543-567).  True for every pair of
+ * {F32, F16, Q8_0, Q5_1, Q5_0, Q4_1, Q4_0} when head_dim == 64 and
+ * n_q_heads is a multiple of n_kv_heads with a ratio of at most 8. */
+int32_t cvattn_supports(int32_t k_type, int32_t v_type, int32_t head_dim,
+                        int32_t n_q_heads, int32_t n_kv_heads);
+
+/* The loader's fallback chain q4_0 -> q4_1 -> q5_0 -> q5_1 -> q8_0 -> f16 -> f32
+ * on ggml ids (src/cosyvoice-loader.cpp:498-510); -1 past f32. */
+int32_t cvattn_kv_fallback_type(int32_t ggml_type);
+
+/* cosyvoice_kv_cache_type_t (include/cosyvoice.h:32-42) <-> ggml type id
+ * (src/cosyvoice-loader.cpp:468-496); -1 for an unknown value. */
+int32_t cvattn_kv_cache_type_to_ggml(int32_t cosyvoice_kv_cache_type);
+int32_t cvattn_ggml_to_kv_cache_type(int32_t ggml_type);
+
+/* Flash-attention branch of cosyvoice_check_kv_cache_types
+ * (src/cosyvoice-loader.cpp:533-632) with cvattn_supports as the probe.
+ * kv_type_union is the packed value of include/cosyvoice.h:193-221
+ * (bit 31 = separate K/V; K bits 0-4, V 5-9, fallback 10-14).
+ * Outputs the resolved ggml K/V types, the rewritten union and whether
+ * flash attention is on. */
+cvattn_status cvattn_negotiate_kv_types(uint32_t kv_type_union, int32_t kv_fallback,
+                                        int32_t head_dim, int32_t n_q_heads, int32_t n_kv_heads,
+                                        int32_t* k_type, int32_t* v_type,
+                                        uint32_t* resolved_union, int32_t* fattn);
+
+/* ----------------------------------------------------------------- context */
+
+typedef struct cvattn_context cvattn_context;
+
+/* One per worker.  Holds the device status word and per-device state. */
+cvattn_status cvattn_context_create(int32_t device, cvattn_context** out);
+void          cvattn_context_destroy(cvattn_context* ctx);
+
+/* Synchronizes the stream, then reads and clears the device status word.
+ * Returns CVATTN_ERR_DEVICE if a kernel skipped a bad index since the last
+ * call; *detail (optional) receives the first recorded code. */
+cvattn_status cvattn_context_sync_status(cvattn_context* ctx, void* stream, int32_t* detail);
+
+/* -------------------------------------------------------------- KV append */
+
+/* Quantize-on-write of new K or V rows: the ggml_set_rows of
+ * cosyvoice_kv_cache::update_cache (src/cosyvoice-kv-cache.cpp:315-316,321-322).
+ *   src    f32 rows of cache->n_heads*cache->head_dim elements:
+ *          row (t, b) at src + t*src_nb1 + b*src_nb2 (bytes)
+ *   pos    device int32 positions: pos[t + b*pos_nb1/4] (pos_nb1 = 0: shared by
+ *          every batch entry, the LLM's 1-D position_ids; otherwise the DiT's
+ *          [S, batch] position tensor, src/cosyvoice-graph.cpp:447-449)
+ * Blocks are bit-identical to ggml's reference quantizers.  A position outside
+ * [0, cache->ne1) is skipped and recorded in the status word. */
+cvattn_status cvattn_kv_append(cvattn_context* ctx, void* stream, const cvattn_tensor* cache,
+                               const float* src, int64_t src_nb1, int64_t src_nb2,
+                               const int32_t* pos, int64_t pos_nb1,
+                               int32_t n_new, int32_t batch);
+
+/* Dequantize rows [0, n_rows) of every batch entry to f32
+ * (dst row (t, b) at dst + (b*n_rows + t)*n_heads*head_dim).  Used for the
+ * offload of a slot to f32 and by tests. */
+cvattn_status cvattn_kv_dequantize(cvattn_context* ctx, void* stream, const cvattn_tensor* cache,
+                                   int32_t n_rows, float* dst);
+
+/* ------------------------------------------------------------------ decode */
+
+enum {
+    CVATTN_DECODE_EMIT_PARTIAL = 1   /* write unnormalized O and (max, sum) instead of O/sum */
+};
+
+/* One decode token per sequence: ggml_flash_attn_ext with n_q = 1 and no mask
+ * (src/cosyvoice-kv-cache.cpp:379-386 via src/cosyvoice-llm.cpp:62), batched
+ * over sequences, optionally fused with the append of that token's K/V row
+ * (src/cosyvoice-kv-cache.cpp:316,322). */
+typedef struct cvattn_decode_params {
+    const float*    q;               /* device f32 [n_seq][n_q_heads][head_dim] */
+    int64_t         q_seq_stride;    /* floats between sequences */
+    float*          out;             /* device f32 [n_seq][n_q_heads][head_dim] */
+    int64_t         out_seq_stride;  /* floats between sequences */
+    cvattn_tensor   k;               /* type/heads/dims/nb1 shared by all sequences;   */
+    cvattn_tensor   v;               /* sequence s rows at data + s*nb2 unless *_seq_ptrs */
+    const uint64_t* k_seq_ptrs;      /* optional device [n_seq]: row-0 address per sequence */
+    const uint64_t* v_seq_ptrs;      /* (separate worker caches); NULL = data + s*nb2 */
+    const int32_t*  kv_len;          /* device [n_seq]: visible keys incl. an appended row */
+    const float*    k_new;           /* optional device f32 [n_seq][n_heads*head_dim]: row */
+    const float*    v_new;           /* written at position kv_len-1 before attending      */
+    float*          partial_ml;      /* EMIT_PARTIAL: device f32 [n_seq][n_q_heads][2] (max, sum) */
+    int32_t         n_seq;
+    int32_t         n_q_heads;
+    int32_t         max_kv_len;      /* host bound on kv_len[] (sizes the grid) */
+    int32_t         flags;
+    float           scale;           /* 1/sqrt(head_dim) in the reference */
+    int32_t         reserved;
+    void*           workspace;       /* device scratch of cvattn_decode_workspace_size bytes, */
+    size_t          workspace_size;  /* zeroed before first use (cvattn_workspace_init)        */
+} cvattn_decode_params;
+
+/* Workspace bytes for cvattn_decode with this type pair and shape (chunk
+ * partials plus one ticket counter per sequence); 0 if unsupported. */
+size_t cvattn_decode_workspace_size(int32_t k_type, int32_t v_type, int32_t n_seq, int32_t max_kv_len,
+                                    int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim);
+
+/* Zero a workspace (once, after allocation).  The kernels leave it zeroed. */
+cvattn_status cvattn_workspace_init(void* stream, void* workspace, size_t bytes);
+
+cvattn_status cvattn_decode(cvattn_context* ctx, void* stream, const cvattn_decode_params* p);
+
+/* Log-sum-exp combine of split partials (cross-GPU split-KV):
+ *   partial_o  f32 [n_parts][n_rows][head_dim] unnormalized
+ *   partial_ml f32 [n_parts][n_rows][2] (max in log2 units, sum)
+ *   out        f32 [n_rows][head_dim] */
+cvattn_status cvattn_combine(void* stream, const float* partial_o, const float* partial_ml,
+                             int32_t n_parts, int32_t n_rows, int32_t head_dim, float* out);
+
+/* ------------------------------------------------- prefill / DiT attention */
+
+enum {
+    CVATTN_MASK_NONE = 0,      /* every key visible (uncached DiT without mask) */
+    CVATTN_MASK_EXPLICIT = 1,  /* additive f16 mask rows (ggml semantics) */
+    CVATTN_MASK_CAUSAL = 2,    /* query i sees key j iff j <= causal_offset + i (src/cosyvoice-llm.cpp:20-29) */
+    CVATTN_MASK_CHUNK = 3      /* DiT streaming chunk mask (src/cosyvoice-token2wav.cpp:285-298) */
+};
+
+#define CVATTN_MAX_CHUNK_BOUNDS 64
+
+/* Multi-query attention: Qwen2 prefill (src/cosyvoice-llm.cpp:62, mask
+ * :101-108) and DiT attention, cached (src/cosyvoice-graph.cpp:363-366) or
+ * uncached (:373-377).  Q is f32 as ggml passes it; K/V are typed cache rows
+ * or uncached f32 activations in the same row layout. */
+typedef struct cvattn_flash_params {
+    const float*    q;            /* device f32; element (d, i, h, b) at          */
+    int64_t         q_nb_tok;     /* q + i*q_nb_tok + h*q_nb_head + b*q_nb_batch + d */
+    int64_t         q_nb_head;    /* (strides in floats)                          */
+    int64_t         q_nb_batch;
+    float*          out;          /* device f32 [batch][n_q][n_q_heads][head_dim] */
+    cvattn_tensor   k;            /* positions [0, n_kv) of batch b at data + b*nb2 */
+    cvattn_tensor   v;
+    int32_t         n_q;
+    int32_t         n_kv;
+    int32_t         n_q_heads;
+    int32_t         batch;
+    float           scale;
+    int32_t         mask_mode;    /* CVATTN_MASK_* */
+    const uint16_t* mask;         /* EXPLICIT: device f16 bits, row i at mask + i*mask_nb1 + b*mask_nb2 */
+    int64_t         mask_nb1;     /* (elements) */
+    int64_t         mask_nb2;
+    int32_t         causal_offset;                 /* CAUSAL: n_kv - n_q for llm_prefill */
+    int32_t         n_chunk_bounds;                /* CHUNK */
+    int32_t         chunk_bounds[CVATTN_MAX_CHUNK_BOUNDS]; /* ascending chunk ends (host values) */
+    int32_t         chunk_key_offset;  /* CHUNK: keys below this are always visible (cached prompt) */
+    int32_t         chunk_row_offset;  /* CHUNK: query i uses mask row i + chunk_row_offset */
+} cvattn_flash_params;
+
+cvattn_status cvattn_flash(cvattn_context* ctx, void* stream, const cvattn_flash_params* p);
+
+/* ------------------------------------------------------- offload and load */
+
+/* Copy positions [0, n_tokens) of every batch entry of a KV tensor to host
+ * memory, batch-major and contiguous (the per-layer K or V part of
+ * cosyvoice_kv_cache::offload_cache, src/cosyvoice-kv-cache.cpp:160-172),
+ * and back (load_cache, :233-243).  host may be pageable or pinned. */
+cvattn_status cvattn_kv_copy_to_host(void* stream, const cvattn_tensor* t, int32_t n_tokens, void* host);
+cvattn_status cvattn_kv_copy_from_host(void* stream, const cvattn_tensor* t, int32_t n_tokens,
+                                       const void* host);
+
+/* -------------------------------------------------- KV cache host object */
+
+/* Host-side mirror of class cosyvoice_kv_cache (src/cosyvoice-kv-cache.h:10-69)
+ * in the flash-attention mode the reference uses by default. */
+typedef struct cvattn_kv_cache cvattn_kv_cache;
+
+typedef struct cvattn_kv_cache_params {
+    int32_t  layers;
+    int32_t  k_head_dim;
+    int32_t  v_head_dim;
+    int32_t  n_kv_heads;
+    uint32_t max_seq;
+    int32_t  k_type;             /* ggml ids */
+    int32_t  v_type;
+    int32_t  batch;
+    int32_t  n_slots;
+    int32_t  n_offloaded_slots;
+} cvattn_kv_cache_params;
+
+/* build_kv_cache (src/cosyvoice-kv-cache.cpp:45-102): one device allocation
+ * holding K then V for every (slot, layer), each 256-byte aligned. */
+cvattn_status cvattn_kv_cache_create(cvattn_context* ctx, const cvattn_kv_cache_params* p,
+                                     cvattn_kv_cache** out);
+void          cvattn_kv_cache_destroy(cvattn_kv_cache* c);
+
+/* The K (which = 0) or V (which = 1) tensor of (layer, slot). */
+cvattn_status cvattn_kv_cache_tensor(cvattn_kv_cache* c, int32_t layer, int32_t slot, int32_t which,
+                                     cvattn_tensor* out);
+size_t        cvattn_kv_cache_device_bytes(const cvattn_kv_cache* c);
+
+/* cur_len and the view length seen by attention. */
+uint32_t      cvattn_kv_cache_get_len(const cvattn_kv_cache* c);
+void          cvattn_kv_cache_set_len(cvattn_kv_cache* c, uint32_t len);
+
+/* update_cache (src/cosyvoice-kv-cache.cpp:309-355): append n_new rows of f32
+ * K and V ([n_heads*head_dim] per row, token-major, batch-major) at device
+ * positions pos (pos_nb1 as in cvattn_kv_append) into the bound slot; the
+ * attention view becomes cur_len + n_new long. */
+cvattn_status cvattn_kv_cache_update(cvattn_kv_cache* c, void* stream, int32_t layer,
+                                     const float* k, const float* v, const int32_t* pos,
+                                     int64_t pos_nb1, int32_t n_new);
+
+/* attention_forward (src/cosyvoice-kv-cache.cpp:379-386) over the current view
+ * of (layer, bound slot).  q f32 [batch][n_q][n_q_heads][head_dim]; scale
+ * 1/sqrt(head_dim); n_q == 1 without a mask runs the decode kernel, anything
+ * else the tensor-core flash kernel.  mask semantics as cvattn_flash_params. */
+cvattn_status cvattn_kv_cache_attention(cvattn_kv_cache* c, void* stream, int32_t layer,
+                                        const float* q, int32_t n_q, int32_t n_q_heads,
+                                        int32_t mask_mode, const uint16_t* mask, int64_t mask_nb1,
+                                        float* out);
+
+/* shift_kv_node_pos (src/cosyvoice-kv-cache.cpp:398-408): cur_len += n. */
+void          cvattn_kv_cache_shift(cvattn_kv_cache* c, uint32_t n);
+
+/* bind_slot / slide_kv_slot (src/cosyvoice-kv-cache.cpp:415-467). */
+int32_t       cvattn_kv_cache_bind_slot(cvattn_kv_cache* c, int32_t slot);
+cvattn_status cvattn_kv_cache_slide_slot(cvattn_kv_cache* c);
+int32_t       cvattn_kv_cache_current_slot(const cvattn_kv_cache* c);
+
+/* offload_slot / load_slot (src/cosyvoice-kv-cache.cpp:148-246,276-290):
+ * positions [0, n_tokens) of every layer of the bound slot to host slot
+ * `offloaded_slot` and back (load restores cur_len).  Synchronous on the
+ * stream, like the reference's ggml_backend_sched_synchronize. */
+cvattn_status cvattn_kv_cache_offload_slot(cvattn_kv_cache* c, void* stream, int32_t offloaded_slot,
+                                           uint32_t n_tokens);
+cvattn_status cvattn_kv_cache_load_slot(cvattn_kv_cache* c, void* stream, int32_t offloaded_slot);
+size_t        cvattn_kv_cache_offloaded_size(const cvattn_kv_cache* c);
+void          cvattn_kv_cache_clear_offloaded(cvattn_kv_cache* c);
+
+/* ------------------------------------------------------- DiT step plan */
+
+/* One ODE step of dit_sched_config (src/cosyvoice-token2wav.cpp:100-167). */
+typedef struct cvattn_dit_step {
+    uint8_t rebuild, cache_kv, load, offload, slide, slice, mask, reserved;
+    int64_t cut_len;
+} cvattn_dit_step;
+
+cvattn_status cvattn_dit_sched_plan(int32_t n_steps, int32_t n_offloadable_slots, int32_t n_fixed_slots,
+                                    int64_t cut_len, uint32_t offset, int32_t streaming,
+                                    int32_t kv_slidable, cvattn_dit_step* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CVATTN_H */
