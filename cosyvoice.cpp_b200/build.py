@@ -39,8 +39,9 @@ def _units():
         obj = os.path.join(BUILD, src.replace(".", "_") + ".o")
         units.append((os.path.join(CSRC, src), obj, []))
     for name, tid in K_TYPES.items():
-        obj = os.path.join(BUILD, f"decode_inst_{name}.o")
-        units.append((os.path.join(CSRC, "decode_inst.cu"), obj, [f"-DCVATTN_KT={tid}"]))
+        for stem in ("decode_inst", "flash_inst"):
+            obj = os.path.join(BUILD, f"{stem}_{name}.o")
+            units.append((os.path.join(CSRC, f"{stem}.cu"), obj, [f"-DCVATTN_KT={tid}"]))
     return units, headers
 
 

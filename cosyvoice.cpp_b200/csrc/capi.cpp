@@ -115,11 +115,10 @@ size_t cvattn_row_size(int32_t type, int64_t n) {
 
 // ------------------------------------------------------- types / capability
 
+// The flash kernel serves every query count; the decode kernel is a faster
+// path for one query row that cvattn_kv_cache_attention picks when it applies.
 int32_t cvattn_supports(int32_t k_type, int32_t v_type, int32_t head_dim, int32_t n_q_heads, int32_t n_kv_heads) {
-    return decode_supported(k_type, v_type, head_dim, n_q_heads, n_kv_heads) &&
-                   flash_supported(k_type, v_type, head_dim, n_q_heads, n_kv_heads)
-               ? 1
-               : 0;
+    return flash_supported(k_type, v_type, head_dim, n_q_heads, n_kv_heads) ? 1 : 0;
 }
 
 // src/cosyvoice-loader.cpp:498-510
@@ -255,7 +254,7 @@ cvattn_status cvattn_context_sync_status(cvattn_context* ctx, void* stream, int3
     if (e == cudaSuccess) e = cudaStreamSynchronize(as_stream(stream));
     if (e != cudaSuccess) return from_cuda(e);
     if (detail) *detail = v;
-    if (v == 3) return CVATTN_ERR_TIMEOUT;
+    if ((v & 0xff) == 3) return CVATTN_ERR_TIMEOUT;
     return v ? CVATTN_ERR_DEVICE : CVATTN_OK;
 }
 
@@ -518,7 +517,8 @@ cvattn_status cvattn_kv_cache_attention(cvattn_kv_cache* c, void* stream, int32_
     const cvattn_tensor vt = cache_tensor(c, layer, c->cur_slot, 1);
     const int32_t n_kv = (int32_t)c->view_len;
     const int64_t D = kt.head_dim;
-    if (n_q == 1 && mask_mode == CVATTN_MASK_NONE) {
+    if (n_q == 1 && mask_mode == CVATTN_MASK_NONE &&
+        decode_supported(kt.type, vt.type, kt.head_dim, n_q_heads, kt.n_heads)) {
         cvattn_decode_params dp{};
         dp.q = q;
         dp.q_seq_stride = n_q_heads * D;

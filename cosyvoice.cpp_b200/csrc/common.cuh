@@ -305,13 +305,38 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait: gives up after ~2^22 polls (each try_wait itself suspends for
-// a hardware-chosen interval), records kStatusTimeout and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
-    for (uint32_t it = 0; it < (1u << 22); ++it)
-        if (mbar_try_wait(bar, parity)) return true;
-    record_status(status, kStatusTimeout);
-    return false;
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// try_wait with an explicit suspend-time hint (ns) so one poll never sleeps long.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns) : "memory");
+    return ok != 0;
+}
+
+// Wall-clock budget of one bounded wait.  A wait that runs out records
+// kStatusTimeout plus its call-site code (status word = 0x100 * site + 3) and
+// returns false; callers then stop issuing work and fall through to teardown.
+constexpr uint64_t kWaitBudgetNs = 2000000000ull;
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int site = 0) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+        if (mbar_try_wait_hint(bar, parity, 1000u)) return true;
+        if (global_timer_ns() - t0 > kWaitBudgetNs) {
+            record_status(status, kStatusTimeout | (site << 8));
+            return false;
+        }
+    }
 }
 
 // ------------------------------------------------------ bulk async copies --

@@ -67,6 +67,7 @@ cudaError_t launch_decode(cudaStream_t stream, const cvattn_decode_params& p, in
     a.G = p.n_q_heads / Hkv;
     a.C = C;
     a.flags = p.flags;
+    a.max_kv_len = p.max_kv_len;
     a.scale_log2 = p.scale * 1.4426950408889634f;
     uint8_t* ws = static_cast<uint8_t*>(p.workspace);
     const size_t cnt_bytes = align256((size_t)p.n_seq * 4);

@@ -52,6 +52,7 @@ struct Args {
     const float* v_new;
     float* partial_ml;
     int n_seq, Hq, Hkv, G, C, flags;
+    int max_kv_len;  // host bound the grid and workspace were sized for
     float scale_log2;
     float* ws_o;
     float* ws_ml;
@@ -181,7 +182,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const Args a) {
 
     const int len = a.kv_len[seq];
     float* out = a.out + (int64_t)seq * a.out_seq_stride;
-    if (len <= 0 || len > a.capacity || len > (int)gridDim.x * C) {
+    if (len <= 0 || len > a.capacity || len > a.max_kv_len) {
         // empty or invalid sequence: zero output, flag invalid lengths
         if (chunk == 0) {
             for (int i = tid; i < Hq * kD; i += kThreads) out[(i / kD) * kD + (i % kD)] = 0.0f;
@@ -246,7 +247,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const Args a) {
         }
     }
 
-    if (!mbar_wait(bar, 0, a.status)) return;
+    if (!mbar_wait(bar, 0, a.status, 1)) return;
     __syncthreads();
 
     // ---- fused append of this step's row (position len-1) into cache and chunk copy

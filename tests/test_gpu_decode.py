@@ -1,0 +1,202 @@
+"""GPU: split-KV decode attention vs the fp64 oracle.
+
+ggml_flash_attn_ext with one query row, no mask, scale 1/sqrt(64), f32
+precision requested (src/cosyvoice-kv-cache.cpp:379-386, via
+src/cosyvoice-llm.cpp:62) on Qwen2 shapes: 14 query heads, 2 KV heads, D=64.
+The kernel computes in fp32 on exactly dequantized K/V, so the bar is the
+north-star's f32 one: relative L2 <= 1e-5 (and max-abs <= 2e-3) against fp64
+attention over the oracle-dequantized cache.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+HQ, HKV, D = 14, 2, 64
+SCALE = 1.0 / 8.0
+REL_L2 = 1e-5
+MAX_ABS = 2e-3
+ALL = ["f32", "f16", "q8_0", "q5_1", "q5_0", "q4_1", "q4_0"]
+
+
+def rel_l2(a, b):
+    return float(np.linalg.norm((a - b).ravel()) / max(np.linalg.norm(b.ravel()), 1e-30))
+
+
+def build(cv, cuda, oracle, kt, vt, lens, rng, cap=None, outliers=False):
+    torch = cuda
+    n_seq = len(lens)
+    cap = cap or max(lens)
+    row = HKV * D
+    kx = rng.standard_normal((n_seq, cap, row)).astype(np.float32)
+    vx = rng.standard_normal((n_seq, cap, row)).astype(np.float32)
+    if outliers:
+        for a in (kx, vx):
+            hit = rng.random(a.shape) < 0.01
+            a[hit] = np.where(rng.random(hit.sum()) < 0.5, -8.0, 8.0)
+    kq, vq = oracle.quantize(kt, kx), oracle.quantize(vt, vx)
+    kbuf = torch.tensor(kq.reshape(-1), device="cuda")
+    vbuf = torch.tensor(vq.reshape(-1), device="cuda")
+    kd = cv.kv_tensor(kbuf, kt, HKV, D, cap, n_seq)
+    vd = cv.kv_tensor(vbuf, vt, HKV, D, cap, n_seq)
+    return kq, vq, kbuf, vbuf, kd, vd
+
+
+def reference(oracle, kt, vt, kq, vq, q, lens):
+    out = np.zeros_like(q)
+    for s, L in enumerate(lens):
+        if L == 0:
+            continue
+        kd = oracle.dequantize(kt, kq[s, :L], HKV * D).reshape(L, HKV, D)
+        vd = oracle.dequantize(vt, vq[s, :L], HKV * D).reshape(L, HKV, D)
+        out[s] = oracle.attention_f64(q[s][None], kd, vd, SCALE)[0]
+    return out
+
+
+@pytest.mark.parametrize("kname", ALL)
+@pytest.mark.parametrize("vname", ALL)
+def test_decode_type_pairs(ctx, cv, cuda, oracle, kname, vname):
+    torch = cuda
+    kt, vt = cv.TYPE_BY_NAME[kname], cv.TYPE_BY_NAME[vname]
+    rng = np.random.default_rng(kt * 16 + vt)
+    lens = [1, 64, 129, 300]
+    kq, vq, kb, vb, kd, vd = build(cv, cuda, oracle, kt, vt, lens, rng, outliers=True)
+    q = rng.standard_normal((len(lens), HQ, D)).astype(np.float32)
+    qt = torch.tensor(q, device="cuda")
+    kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    out = cv.decode(ctx, qt, kd, vd, kl, max(lens)).cpu().numpy()
+    ref = reference(oracle, kt, vt, kq, vq, q, lens)
+    assert rel_l2(out, ref) <= REL_L2, f"{kname}/{vname} rel-L2 {rel_l2(out, ref):.3e}"
+    assert np.abs(out - ref).max() <= MAX_ABS
+
+
+@pytest.mark.parametrize("kname,vname", [("q8_0", "q8_0"), ("q8_0", "q4_0"), ("q5_1", "q5_1"), ("f16", "f16")])
+def test_decode_mixed_lengths_64_sequences(ctx, cv, cuda, oracle, kname, vname):
+    """The benchmark mix: 64 sequences, lengths U[128, 2048] (seed 0)."""
+    torch = cuda
+    kt, vt = cv.TYPE_BY_NAME[kname], cv.TYPE_BY_NAME[vname]
+    lens = np.random.default_rng(0).integers(128, 2049, 64).tolist()
+    rng = np.random.default_rng(11)
+    kq, vq, kb, vb, kd, vd = build(cv, cuda, oracle, kt, vt, lens, rng, cap=2048)
+    q = rng.standard_normal((64, HQ, D)).astype(np.float32)
+    kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, 2048).cpu().numpy()
+    ref = reference(oracle, kt, vt, kq, vq, q, lens)
+    assert rel_l2(out, ref) <= REL_L2
+    assert np.abs(out - ref).max() <= MAX_ABS
+
+
+@pytest.mark.parametrize("kname,vname", [("q8_0", "q8_0"), ("q5_1", "q4_1"), ("f16", "q5_0"), ("f32", "f32")])
+def test_decode_fused_append(ctx, cv, cuda, oracle, kname, vname):
+    """The step's K/V row is quantized into the cache at kv_len-1 and attended to."""
+    torch = cuda
+    kt, vt = cv.TYPE_BY_NAME[kname], cv.TYPE_BY_NAME[vname]
+    rng = np.random.default_rng(21)
+    lens = [1, 128, 129, 257, 700]
+    cap = 768
+    kq, vq, kb, vb, kd, vd = build(cv, cuda, oracle, kt, vt, lens, rng, cap=cap)
+    n = len(lens)
+    knew = rng.standard_normal((n, HKV * D)).astype(np.float32)
+    vnew = rng.standard_normal((n, HKV * D)).astype(np.float32)
+    q = rng.standard_normal((n, HQ, D)).astype(np.float32)
+    kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, max(lens),
+                    k_new=torch.tensor(knew, device="cuda"), v_new=torch.tensor(vnew, device="cuda")).cpu().numpy()
+    kq2, vq2 = kq.copy(), vq.copy()
+    for s, L in enumerate(lens):
+        kq2[s, L - 1] = oracle.quantize(kt, knew[s:s + 1])[0]
+        vq2[s, L - 1] = oracle.quantize(vt, vnew[s:s + 1])[0]
+    kgot = kb.view(n, cap, -1).cpu().numpy()
+    vgot = vb.view(n, cap, -1).cpu().numpy()
+    assert np.array_equal(kgot, kq2) and np.array_equal(vgot, vq2), "appended rows differ from the oracle"
+    ref = reference(oracle, kt, vt, kq2, vq2, q, lens)
+    assert rel_l2(out, ref) <= REL_L2
+
+
+def test_decode_separate_worker_buffers(ctx, cv, cuda, oracle):
+    """Per-sequence row pointers: each worker owns its own cache buffer."""
+    torch = cuda
+    kt = vt = cv.Q8_0
+    rng = np.random.default_rng(7)
+    lens = [100, 1000, 513]
+    bufs, kqs, vqs = [], [], []
+    for L in lens:
+        kx = rng.standard_normal((L, HKV * D)).astype(np.float32)
+        vx = rng.standard_normal((L, HKV * D)).astype(np.float32)
+        kq, vq = oracle.quantize(kt, kx), oracle.quantize(vt, vx)
+        kqs.append(kq)
+        vqs.append(vq)
+        bufs.append((torch.tensor(kq.reshape(-1), device="cuda"), torch.tensor(vq.reshape(-1), device="cuda")))
+    kp = torch.tensor([b[0].data_ptr() for b in bufs], dtype=torch.int64, device="cuda")
+    vp = torch.tensor([b[1].data_ptr() for b in bufs], dtype=torch.int64, device="cuda")
+    desc_k = cv.kv_tensor(bufs[0][0], kt, HKV, D, max(lens), len(lens))
+    desc_v = cv.kv_tensor(bufs[0][1], vt, HKV, D, max(lens), len(lens))
+    q = rng.standard_normal((len(lens), HQ, D)).astype(np.float32)
+    kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    out = cv.decode(ctx, torch.tensor(q, device="cuda"), desc_k, desc_v, kl, max(lens),
+                    k_seq_ptrs=kp, v_seq_ptrs=vp).cpu().numpy()
+    for s, L in enumerate(lens):
+        kd = oracle.dequantize(kt, kqs[s], HKV * D).reshape(L, HKV, D)
+        vd = oracle.dequantize(vt, vqs[s], HKV * D).reshape(L, HKV, D)
+        ref = oracle.attention_f64(q[s][None], kd, vd, SCALE)[0]
+        assert rel_l2(out[s], ref) <= REL_L2
+
+
+def test_decode_split_partials_and_combine(ctx, cv, cuda, oracle):
+    """Long-context split-KV: two position shards emit partials, combine merges them."""
+    torch = cuda
+    kt, vt = cv.Q8_0, cv.Q4_0
+    rng = np.random.default_rng(9)
+    L = 3000
+    cut = 1216
+    kq, vq, kb, vb, kd, vd = build(cv, cuda, oracle, kt, vt, [L], rng)
+    q = rng.standard_normal((1, HQ, D)).astype(np.float32)
+    qt = torch.tensor(q, device="cuda")
+    rbk, rbv = cv.row_size(kt, 128), cv.row_size(vt, 128)
+    po = torch.empty((2, HQ, D), dtype=torch.float32, device="cuda")
+    pml = torch.empty((2, HQ, 2), dtype=torch.float32, device="cuda")
+    for part, (start, n) in enumerate([(0, cut), (cut, L - cut)]):
+        kp = torch.tensor([kb.data_ptr() + start * rbk], dtype=torch.int64, device="cuda")
+        vp = torch.tensor([vb.data_ptr() + start * rbv], dtype=torch.int64, device="cuda")
+        kl = torch.tensor([n], dtype=torch.int32, device="cuda")
+        cv.decode(ctx, qt, kd, vd, kl, n, out=po[part:part + 1], k_seq_ptrs=kp, v_seq_ptrs=vp,
+                  emit_partial=True, partial_ml=pml[part:part + 1])
+    out = cv.combine(po, pml).cpu().numpy().reshape(1, HQ, D)
+    ref = reference(oracle, kt, vt, kq, vq, q, [L])
+    assert rel_l2(out, ref) <= REL_L2
+
+
+def test_decode_zero_and_invalid_lengths(ctx, cv, cuda, oracle):
+    torch = cuda
+    kt = vt = cv.Q8_0
+    rng = np.random.default_rng(13)
+    kq, vq, kb, vb, kd, vd = build(cv, cuda, oracle, kt, vt, [200, 200, 200], rng)
+    q = torch.tensor(rng.standard_normal((3, HQ, D)).astype(np.float32), device="cuda")
+    # seq 0 empty -> zeros; seq 2 longer than the launch bound -> zeros + status
+    kl = torch.tensor([0, 150, 190], dtype=torch.int32, device="cuda")
+    out = cv.decode(ctx, q, kd, vd, kl, 160).cpu().numpy()
+    assert not out[0].any() and not out[2].any()
+    assert np.abs(out[1]).sum() > 0
+    st, detail = ctx.sync_status()
+    assert st == 6 and detail == 2
+
+
+def test_decode_workspace_reuse_many_calls(ctx, cv, cuda, oracle):
+    """The ticket counters return to zero: repeated calls on one workspace agree."""
+    torch = cuda
+    kt = vt = cv.Q8_0
+    rng = np.random.default_rng(17)
+    lens = [1500, 700, 2048, 129]
+    kq, vq, kb, vb, kd, vd = build(cv, cuda, oracle, kt, vt, lens, rng)
+    q = torch.tensor(rng.standard_normal((4, HQ, D)).astype(np.float32), device="cuda")
+    kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    out = torch.empty_like(q)
+    dec = cv.Decoder(ctx, kd, vd, 4, HQ, 2048, q, out, kl)
+    dec()
+    first = out.clone()
+    for _ in range(20):
+        dec()
+    torch.cuda.synchronize()
+    assert torch.equal(first, out)
