@@ -1,0 +1,498 @@
+"""Benchmark of the cvattn engine on the reference's headline workload.
+
+Headline (N=1): Qwen2-0.5B-shaped LLM decode
+attention over all 24 layers, q8_0 KV cache (ggml blocks), 64 concurrent
+sequences with context lengths U[128, 2048] (numpy default_rng(0), sum 70,843),
+K/V ~ N(0,1) before quantization.  One step = every layer's fused
+append-of-the-new-token + split-KV attention for all 64 sequences, launched
+as one CUDA graph of 24 kernels.  metric = KV bytes streamed by attention per
+second (GB/s, whole job); tok/s = sequences x steps / s.
+
+Multi-GPU (torchrun, one process per GPU): every rank serves its own 64
+sequences (weak scaling: requests shard by sequence, no collective on the
+path); time = max over ranks of the CUDA-event time.
+
+--impl reference times the reference's CPU attention path restated by the
+oracle (ggml is not available to build) on the host cores, on a bounded
+sample of the same workload.
+
+Secondary figures in the same JSON line: DiT attention TFLOP/s
+and causal prefill TFLOP/s from the tcgen05 flash kernel.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "cosyvoice.cpp_b200"))
+sys.path.insert(0, ROOT)
+
+HQ, HKV, D, LAYERS, N_SEQ, CAP = 14, 2, 64, 24, 64, 2048
+METRIC = "LLM decode-attn KV GB/s + tok/s (frac HBM peak); DiT attn TFLOP/s at 1/2/4/8 GPU"
+WORKLOAD = "qwen2-0.5b decode attention, 24 layers, q8_0 KV, 64 seqs, L~U[128,2048] (seed 0)"
+
+
+def seq_lengths() -> list[int]:
+    return np.random.default_rng(0).integers(128, 2049, N_SEQ).tolist()
+
+
+def measured_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def profiled_traffic() -> dict:
+    """Per-launch DRAM bytes of the dominant kernels from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi SM clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ our arm
+
+def build_decode_workload_layers(torch, cv, ctx, n_layers: int):
+    return build_decode_workload(torch, cv, ctx, cv.Q8_0, 0, n_layers)
+
+
+def build_decode_workload(torch, cv, ctx, kv_type: int, rank: int, n_layers: int = LAYERS):
+    """Device-resident q8_0 caches for n_layers x 64 sequences (seeded)."""
+    lens = seq_lengths()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1234 + rank)
+    caches = []
+    pos = torch.arange(CAP, dtype=torch.int32, device="cuda")
+    for layer in range(n_layers):
+        kb, kd = cv.alloc_kv(kv_type, HKV, D, CAP, N_SEQ)
+        vb, vd = cv.alloc_kv(kv_type, HKV, D, CAP, N_SEQ)
+        for buf_desc in (kd, vd):
+            x = torch.randn(N_SEQ, CAP, HKV * D, device="cuda", generator=gen)
+            cv.kv_append(ctx, buf_desc, x, pos)   # quantize-on-write, bit-exact ggml blocks
+            del x
+        caches.append((kb, kd, vb, vd))
+    torch.cuda.synchronize()
+    q = torch.randn(n_layers, N_SEQ, HQ, D, device="cuda", generator=gen)
+    k_new = torch.randn(n_layers, N_SEQ, HKV * D, device="cuda", generator=gen)
+    v_new = torch.randn(n_layers, N_SEQ, HKV * D, device="cuda", generator=gen)
+    out = torch.empty_like(q)
+    kv_len = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    return lens, caches, q, k_new, v_new, out, kv_len
+
+
+def run_ours(args, rank: int, world: int, torch, dist) -> dict | None:
+    import cvattn as cv
+    dev = torch.cuda.current_device()
+    ctx = cv.Context(dev)
+    kv_type = cv.Q8_0
+    lens, caches, q, k_new, v_new, out, kv_len = build_decode_workload(torch, cv, ctx, kv_type, rank)
+    row = cv.row_size(kv_type, HKV * D)
+    bytes_per_layer = sum(lens) * 2 * row            # K and V rows read by attention
+    bytes_per_step = bytes_per_layer * LAYERS
+    decs = [cv.Decoder(ctx, caches[l][1], caches[l][3], N_SEQ, HQ, CAP, q[l], out[l], kv_len,
+                       k_new=k_new[l], v_new=v_new[l]) for l in range(LAYERS)]
+    stream = torch.cuda.Stream()
+
+    def step(s):
+        for d in decs:
+            d(s)
+
+    # warm-up and CUDA-graph capture of one step (24 launches)
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            step(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        graph.capture_begin()
+        step(stream)
+        graph.capture_end()
+    torch.cuda.synchronize()
+    st, detail = ctx.sync_status()
+    if st != 0:
+        raise RuntimeError(f"device status {st} ({detail}) after warm-up")
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- device-resident timed region
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(args.warmup):
+        graph.replay()
+    barrier()
+    with ClockSampler(dev) as clocks:
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+        e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    barrier()
+    ms_max = ms
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    ms_per_step = ms_max / args.steps
+
+    # ---- per-launch duration of the dominant kernel (decode), events on its stream
+    n_launch = 48
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_launch)]
+    with torch.cuda.stream(stream):
+        for i in range(n_launch):
+            evs[i][0].record(stream)
+            decs[i % LAYERS](stream)
+            evs[i][1].record(stream)
+    torch.cuda.synchronize()
+    launch_us = 1000.0 * statistics.mean(a.elapsed_time(b) for a, b in evs)
+
+    # ---- end to end through the C ABI: host Q/K/V rows in, outputs back to host
+    hq = torch.empty_like(q, device="cpu").pin_memory()
+    hk = torch.empty_like(k_new, device="cpu").pin_memory()
+    hv = torch.empty_like(v_new, device="cpu").pin_memory()
+    hout = torch.empty_like(out, device="cpu").pin_memory()
+    hq.copy_(q.cpu()); hk.copy_(k_new.cpu()); hv.copy_(v_new.cpu())
+    h2d = hq.numel() * 4 + hk.numel() * 4 + hv.numel() * 4
+    d2h = hout.numel() * 4
+
+    def e2e_step(s):
+        q.copy_(hq, non_blocking=True)
+        k_new.copy_(hk, non_blocking=True)
+        v_new.copy_(hv, non_blocking=True)
+        step(s)
+        hout.copy_(out, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            e2e_step(stream)
+    barrier()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step(stream)
+        e1.record(stream)
+    e1.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_ms_per_step = e2e_ms / args.steps
+    st, detail = ctx.sync_status()
+    if st != 0:
+        raise RuntimeError(f"device status {st} ({detail}) after the timed region")
+
+    secondary = {}
+    if rank == 0 and not args.skip_secondary:
+        secondary = run_flash_secondary(torch, cv, ctx, args)
+    del graph
+    if rank != 0:
+        return None
+
+    peaks = measured_peaks()
+    value = world * bytes_per_step / (ms_per_step * 1e-3) / 1e9
+    achieved = bytes_per_layer / (launch_us * 1e-6) / 1e9
+    traffic = profiled_traffic().get("decode_q8_0_mix_per_launch")
+    return {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) K/V quantized to q8_0 by the engine's bit-exact append)",
+        "config": {"workload": WORKLOAD, "layers": LAYERS, "n_seq_per_gpu": N_SEQ, "q_heads": HQ,
+                   "kv_heads": HKV, "head_dim": D, "kv_type": "q8_0", "sum_kv_len": sum(lens),
+                   "kv_bytes_per_step": bytes_per_step,
+                   "l2": "inputs larger than L2: %.0f MB of KV per step vs 126 MB L2" % (bytes_per_step / 1e6),
+                   "step": "CUDA graph of 24 fused append+attention launches",
+                   "parallelism": f"sequence-sharded x{world}"},
+        "tok_per_s": round(world * N_SEQ / (ms_per_step * 1e-3), 1),
+        "frac_hbm_peak": round(value / world / peaks["hbm_gbs"], 4),
+        "e2e": {"value": round(world * bytes_per_step / (e2e_ms_per_step * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms_per_step, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "cvattn_decode via the C ABI; pinned host Q/K/V rows in, outputs back each step"},
+        "roofline": {"bound": "hbm", "kernel": "decode_kernel<q8_0,q8_0,7>", "achieved": round(achieved, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "peak_source": peaks["source"], "launch_us": round(launch_us, 3),
+                     "algorithmic_bytes_per_launch": bytes_per_layer, "traffic": traffic},
+        "gpu_launches": args.steps * LAYERS,
+        "clocks": clocks.summary(),
+        **secondary,
+    }
+
+
+def run_flash_secondary(torch, cv, ctx, args, only: str | None = None, reps: int = 10) -> dict:
+    """DiT attention and causal prefill TFLOP/s."""
+    res = {}
+    peaks = measured_peaks()
+    if only == "prefill":
+        return _prefill_part(torch, cv, ctx, peaks, res, reps)
+    # --- DiT: H=16, D=64, 600 queries, 300 cached prompt + 600 current keys,
+    # 50-frame chunk mask, CFG batch 2 x 32 utterances in one launch (f16 KV).
+    B, H, P, S = 64, 16, 300, 600
+    n_kv = P + S
+    kb, kd = cv.alloc_kv(cv.F16, H, D, 1024, B)
+    vb, vd = cv.alloc_kv(cv.F16, H, D, 1024, B)
+    pos = torch.arange(n_kv, dtype=torch.int32, device="cuda")
+    cv.kv_append(ctx, kd, torch.randn(B, n_kv, H * D, device="cuda"), pos)
+    cv.kv_append(ctx, vd, torch.randn(B, n_kv, H * D, device="cuda"), pos)
+    q = torch.randn(B, S, H, D, device="cuda")
+    out = torch.empty_like(q)
+    bounds = list(range(50, S + 1, 50))
+    visible = S * P + sum(min(next(b for b in bounds if b > i), S) for i in range(S))
+    flops = 4.0 * D * H * B * visible
+    p = cv.flash_params(q, kd, vd, n_kv, out, mask_mode=cv.MASK_CHUNK, chunk_bounds=bounds, chunk_key_offset=P)
+    res["dit"] = _time_flash(torch, cv, ctx, p, flops, peaks, "dit layer, 32 utt x CFG2 per launch",
+                             {"utterances": 32, "cfg": 2, "q_frames": S, "prompt_frames": P, "chunk": 50,
+                              "visible_pairs_per_head": visible, "kv_type": "f16"}, reps)
+    if only == "dit":
+        return res
+    # unmasked 600x600 peak-efficiency point
+    p2 = cv.flash_params(q, kd, vd, S, out)
+    res["dit_unmasked"] = _time_flash(torch, cv, ctx, p2, 4.0 * D * H * B * S * S, peaks, "dit 600x600 unmasked",
+                                      {"utterances": 32, "cfg": 2, "frames": S}, reps)
+    del kb, vb
+    return _prefill_part(torch, cv, ctx, peaks, res, reps)
+
+
+def _prefill_part(torch, cv, ctx, peaks, res, reps) -> dict:
+    # --- causal prefill S=4096, batch 8, Hq 14 / Hkv 2, f16 cache
+    B2, S2 = 8, 4096
+    kb2, kd2 = cv.alloc_kv(cv.F16, HKV, D, S2, B2)
+    vb2, vd2 = cv.alloc_kv(cv.F16, HKV, D, S2, B2)
+    pos2 = torch.arange(S2, dtype=torch.int32, device="cuda")
+    cv.kv_append(ctx, kd2, torch.randn(B2, S2, HKV * D, device="cuda"), pos2)
+    cv.kv_append(ctx, vd2, torch.randn(B2, S2, HKV * D, device="cuda"), pos2)
+    q2 = torch.randn(B2, S2, HQ, D, device="cuda")
+    out2 = torch.empty_like(q2)
+    p3 = cv.flash_params(q2, kd2, vd2, S2, out2, mask_mode=cv.MASK_CAUSAL)
+    res["prefill"] = _time_flash(torch, cv, ctx, p3, 4.0 * D * HQ * B2 * S2 * (S2 + 1) / 2, peaks,
+                                 "causal prefill S=4096 batch 8 (one layer)", {"seq": S2, "batch": B2, "kv_type": "f16"},
+                                 reps)
+    return res
+
+
+def _time_flash(torch, cv, ctx, params, flops, peaks, what, cfg, reps: int = 10) -> dict:
+    import ctypes
+    def launch():
+        cv.check(cv.lib.cvattn_flash(ctx.handle, torch.cuda.current_stream().cuda_stream, ctypes.byref(params)), what)
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        launch()
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / reps
+    tflops = flops / (us * 1e-6) / 1e12
+    return {"what": what, "tflops": round(tflops, 1), "us_per_launch": round(us, 2), "flops_per_launch": flops,
+            "frac_bf16_peak": round(tflops / peaks["bf16_tflops"], 4), "peak_tflops": peaks["bf16_tflops"],
+            "peak_source": peaks["source"], "config": cfg}
+
+
+# ------------------------------------------------------------ reference arm
+
+def _reference_sample():
+    """All 64 sequences of the mix, one layer, q8_0 rows quantized by the oracle."""
+    from oracle import oracle as O
+    O.build()
+    lens = seq_lengths()
+    rng = np.random.default_rng(7)
+    k_rows = [O.quantize(O.Q8_0, rng.standard_normal((L, HKV * D)).astype(np.float32)) for L in lens]
+    v_rows = [O.quantize(O.Q8_0, rng.standard_normal((L, HKV * D)).astype(np.float32)) for L in lens]
+    q = rng.standard_normal((N_SEQ, 1, HQ, D)).astype(np.float32)
+    kl = np.array(lens, np.int32)
+    sample_bytes = int(kl.sum()) * 2 * O.row_bytes(O.Q8_0, HKV * D)
+    threads = os.cpu_count() or 1
+
+    def run():
+        O.flash_cpu(q, k_rows, v_rows, O.Q8_0, O.Q8_0, HKV, kl, False, 0.125, n_threads=threads)
+    return run, sample_bytes, threads
+
+
+SAMPLE_DESC = ("all 64 sequences of the mix (70,843 keys), one of the 24 layers, per sample; "
+               "ggml-CPU-style restatement oracle/cvattn_oracle.c (ggml itself is unavailable)")
+
+
+def run_reference(args) -> dict:
+    """The reference's CPU flash_attn_ext path (oracle restatement), all host threads."""
+    run, sample_bytes, threads = _reference_sample()
+    for _ in range(max(1, args.warmup)):
+        run()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    gbs = sample_bytes / sec / 1e9
+    step_s = sample_bytes * LAYERS / (gbs * 1e9)
+    return {
+        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": WORKLOAD, "kv_type": "q8_0", "layers": LAYERS, "n_seq_per_gpu": N_SEQ},
+        "tok_per_s": round(N_SEQ / step_s, 3),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": SAMPLE_DESC},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def cpu_baseline_for_line(budget_s: float = 10.0) -> dict:
+    """The oracle's CPU path timed for about budget_s on the host cores (rank 0, N=1)."""
+    run, sample_bytes, threads = _reference_sample()
+    run()
+    times, t_end = [], time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    gbs = sample_bytes / statistics.median(times) / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{len(times)} samples of {SAMPLE_DESC}"}
+
+
+def run_profile(args, torch) -> None:
+    """Launch one kernel of the benchmark workload args.steps times, untimed."""
+    import cvattn as cv
+    ctx = cv.Context(torch.cuda.current_device())
+    if args.profile == "decode":
+        # the headline layer shape: one layer's caches, 64 sequences
+        lens, caches, q, k_new, v_new, out, kv_len = build_decode_workload_layers(torch, cv, ctx, 1)
+        dec = cv.Decoder(ctx, caches[0][1], caches[0][3], N_SEQ, HQ, CAP, q[0], out[0], kv_len,
+                         k_new=k_new[0], v_new=v_new[0])
+        for _ in range(args.steps):
+            dec()
+    else:
+        res = run_flash_secondary(torch, cv, ctx, args, only=args.profile, reps=args.steps)
+    torch.cuda.synchronize()
+    st, detail = ctx.sync_status()
+    if st != 0:
+        raise RuntimeError(f"device status {st} ({detail})")
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--skip-secondary", action="store_true", help="skip the DiT / prefill flash figures")
+    ap.add_argument("--profile", choices=["decode", "dit", "prefill"], default=None,
+                    help="only launch the named kernel a few times (for an ncu capture); prints nothing")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return
+
+    import torch
+    dist = None
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    if args.profile:
+        run_profile(args, torch)
+        return
+    res = run_ours(args, rank, world, torch, dist)
+    if rank == 0:
+        if world == 1:
+            res["cpu_baseline"] = cpu_baseline_for_line()
+        print(json.dumps(res), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

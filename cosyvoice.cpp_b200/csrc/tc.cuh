@@ -21,10 +21,10 @@
 namespace cvattn {
 namespace tc {
 
-__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool b_mn_major) {
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool b_mn_major, bool a_mn_major = false) {
     return (1u << 4)                       // D = f32
            | (0u << 7) | (0u << 10)        // A, B = f16
-           | (0u << 15)                    // A K-major
+           | ((a_mn_major ? 1u : 0u) << 15)
            | ((b_mn_major ? 1u : 0u) << 16)
            | ((uint32_t)(N >> 3) << 17)
            | ((uint32_t)(M >> 4) << 24);
@@ -85,6 +85,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
