@@ -35,7 +35,7 @@ def _units():
     units = []
     headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
     headers.append(os.path.join(INCLUDE, "cvattn.h"))
-    for src in ("kv_append.cu", "decode.cu", "flash_tc.cu", "capi.cpp"):
+    for src in ("kv_append.cu", "decode.cu", "flash_tc.cu", "capi.cpp", "decode_noalloc.cu"):
         obj = os.path.join(BUILD, src.replace(".", "_") + ".o")
         units.append((os.path.join(CSRC, src), obj, []))
     for name, tid in K_TYPES.items():

@@ -89,6 +89,7 @@ SIGNATURES = [
     ("cvattn_decode_workspace_size", c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32]),
     ("cvattn_workspace_init", c_int32, [c_void_p, c_void_p, c_size_t]),
     ("cvattn_decode", c_int32, [c_void_p, c_void_p, P(DecodeParams)]),
+    ("cvattn_decode_noalloc", c_int32, [c_void_p, c_void_p, P(DecodeParams)]),
     ("cvattn_combine", c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p]),
     ("cvattn_flash", c_int32, [c_void_p, c_void_p, P(FlashParams)]),
     ("cvattn_kv_copy_to_host", c_int32, [c_void_p, P(Tensor), c_int32, c_void_p]),

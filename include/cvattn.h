@@ -189,6 +189,27 @@ cvattn_status cvattn_workspace_init(void* stream, void* workspace, size_t bytes)
 
 cvattn_status cvattn_decode(cvattn_context* ctx, void* stream, const cvattn_decode_params* p);
 
+/* cvattn_decode for callers that cannot allocate device memory.  This entry
+ * point has no counterpart in the reference.  Examples of such callers: a
+ * ggml custom-op callback that runs inside a scheduled graph compute and
+ * receives only its tensors, or a real-time worker that must not block on
+ * the driver's allocator.
+ * Inputs and outputs are the caller's, as for cvattn_decode; the workspace
+ * fields of p are ignored.  The split-KV partials and ticket counters live
+ * instead in a static device array of CVATTN_DECODE_NOALLOC_SCRATCH_BYTES,
+ * which every GPU that loads the library holds until the process exits.
+ *   - Requests needing more than that (cvattn_decode_workspace_size) return
+ *     CVATTN_ERR_LENGTH and launch nothing.
+ *   - No cudaMalloc/cudaFree is called.  The first call on a device, made
+ *     with that device current, looks up the array's device address; make
+ *     that first call before any stream capture.
+ *   - All calls on a device share the array: calls whose kernels overlap on
+ *     the GPU race and must be serialized.  The ticket counters are zeroed on
+ *     the stream at the start of every call; partials from the previous call
+ *     remain in the array. */
+#define CVATTN_DECODE_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
+cvattn_status cvattn_decode_noalloc(cvattn_context* ctx, void* stream, const cvattn_decode_params* p);
+
 /* Log-sum-exp combine of split partials (cross-GPU split-KV):
  *   partial_o  f32 [n_parts][n_rows][head_dim] unnormalized
  *   partial_ml f32 [n_parts][n_rows][2] (max in log2 units, sum)
