@@ -55,9 +55,10 @@ def reference(oracle, kt, vt, kq, vq, q, lens):
     return out
 
 
+@pytest.mark.parametrize("path", ["tensor_cores", "cuda_cores"])
 @pytest.mark.parametrize("kname", ALL)
 @pytest.mark.parametrize("vname", ALL)
-def test_decode_type_pairs(ctx, cv, cuda, oracle, kname, vname):
+def test_decode_type_pairs(ctx, cv, cuda, oracle, kname, vname, path):
     torch = cuda
     kt, vt = cv.TYPE_BY_NAME[kname], cv.TYPE_BY_NAME[vname]
     rng = np.random.default_rng(kt * 16 + vt)
@@ -66,14 +67,15 @@ def test_decode_type_pairs(ctx, cv, cuda, oracle, kname, vname):
     q = rng.standard_normal((len(lens), HQ, D)).astype(np.float32)
     qt = torch.tensor(q, device="cuda")
     kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
-    out = cv.decode(ctx, qt, kd, vd, kl, max(lens)).cpu().numpy()
+    out = cv.decode(ctx, qt, kd, vd, kl, max(lens), cuda_cores=(path == "cuda_cores")).cpu().numpy()
     ref = reference(oracle, kt, vt, kq, vq, q, lens)
-    assert rel_l2(out, ref) <= REL_L2, f"{kname}/{vname} rel-L2 {rel_l2(out, ref):.3e}"
+    assert rel_l2(out, ref) <= REL_L2, f"{kname}/{vname} {path} rel-L2 {rel_l2(out, ref):.3e}"
     assert np.abs(out - ref).max() <= MAX_ABS
 
 
+@pytest.mark.parametrize("path", ["tensor_cores", "cuda_cores"])
 @pytest.mark.parametrize("kname,vname", [("q8_0", "q8_0"), ("q8_0", "q4_0"), ("q5_1", "q5_1"), ("f16", "f16")])
-def test_decode_mixed_lengths_64_sequences(ctx, cv, cuda, oracle, kname, vname):
+def test_decode_mixed_lengths_64_sequences(ctx, cv, cuda, oracle, kname, vname, path):
     """The benchmark mix: 64 sequences, lengths U[128, 2048] (seed 0)."""
     torch = cuda
     kt, vt = cv.TYPE_BY_NAME[kname], cv.TYPE_BY_NAME[vname]
@@ -82,7 +84,8 @@ def test_decode_mixed_lengths_64_sequences(ctx, cv, cuda, oracle, kname, vname):
     kq, vq, kb, vb, kd, vd = build(cv, cuda, oracle, kt, vt, lens, rng, cap=2048)
     q = rng.standard_normal((64, HQ, D)).astype(np.float32)
     kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
-    out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, 2048).cpu().numpy()
+    out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, 2048,
+                    cuda_cores=(path == "cuda_cores")).cpu().numpy()
     ref = reference(oracle, kt, vt, kq, vq, q, lens)
     assert rel_l2(out, ref) <= REL_L2
     assert np.abs(out - ref).max() <= MAX_ABS
@@ -200,3 +203,23 @@ def test_decode_workspace_reuse_many_calls(ctx, cv, cuda, oracle):
         dec()
     torch.cuda.synchronize()
     assert torch.equal(first, out)
+
+
+@pytest.mark.parametrize("qscale,vscale", [(1e-3, 1.0), (300.0, 1.0), (1.0, 1e3), (1.0, 1e-4)])
+def test_decode_tensor_core_scaling_extremes(ctx, cv, cuda, oracle, qscale, vscale):
+    """Q and V magnitudes far from 1 keep the f32 bar (exact power-of-two scaling of the hi/lo splits)."""
+    torch = cuda
+    kt, vt = cv.Q8_0, cv.Q5_1
+    rng = np.random.default_rng(31)
+    lens = [77, 600]
+    cap = 600
+    kx = rng.standard_normal((2, cap, HKV * D)).astype(np.float32)
+    vx = (rng.standard_normal((2, cap, HKV * D)) * vscale).astype(np.float32)
+    kq, vq = oracle.quantize(kt, kx), oracle.quantize(vt, vx)
+    kd = cv.kv_tensor(torch.tensor(kq.reshape(-1), device="cuda"), kt, HKV, D, cap, 2)
+    vd = cv.kv_tensor(torch.tensor(vq.reshape(-1), device="cuda"), vt, HKV, D, cap, 2)
+    q = (rng.standard_normal((2, HQ, D)) * qscale).astype(np.float32)
+    kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, cap).cpu().numpy()
+    ref = reference(oracle, kt, vt, kq, vq, q, lens)
+    assert rel_l2(out, ref) <= REL_L2, f"rel-L2 {rel_l2(out, ref):.3e}"
