@@ -315,8 +315,9 @@ cvattn_status cvattn_decode(cvattn_context* ctx, void* stream, const cvattn_deco
     if ((p->flags & CVATTN_DECODE_EMIT_PARTIAL) && !p->partial_ml) return CVATTN_ERR_INVALID_ARGUMENT;
     if (p->q_seq_stride < (int64_t)p->n_q_heads * k.head_dim || p->out_seq_stride < (int64_t)p->n_q_heads * k.head_dim)
         return CVATTN_ERR_INVALID_ARGUMENT;
-    if ((reinterpret_cast<uintptr_t>(p->q) & 7) || (reinterpret_cast<uintptr_t>(p->out) & 7) || (p->q_seq_stride & 1) ||
-        (p->out_seq_stride & 1))
+    // q and out rows are accessed as 16-byte vectors
+    if ((reinterpret_cast<uintptr_t>(p->q) & 15) || (reinterpret_cast<uintptr_t>(p->out) & 15) || (p->q_seq_stride & 3) ||
+        (p->out_seq_stride & 3))
         return CVATTN_ERR_INVALID_ARGUMENT;
     const size_t need = decode_workspace_bytes(k.type, v.type, p->n_seq, p->max_kv_len, p->n_q_heads, k.n_heads,
                                                k.head_dim);

@@ -166,6 +166,59 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+// Log-sum-exp merge of one sequence's chunk partials by the CTA that finished
+// last.  All (head, chunk) statistics are fetched in one parallel pass into
+// shared memory (independent L2 loads), then every output element sums its
+// chunks with independent loads.  scratch: >= Hq * (nchunks + 2) floats.
+__device__ __forceinline__ void combine_chunks(const Args& a, int seq, int nchunks, float* out, float* scratch) {
+    const int Hq = a.Hq, tid = threadIdx.x, nt = blockDim.x;
+    const bool emit_partial = (a.flags & CVATTN_DECODE_EMIT_PARTIAL) != 0;
+    float* W = scratch;                      // [Hq][nchunks]: m_c, then weights
+    float* Lc = scratch + Hq * nchunks;      // [Hq][nchunks]: l_c
+    float* MLc = Lc + Hq * nchunks;          // [Hq][2]: M, L
+    const float* seq_ml = a.ws_ml + ((int64_t)seq * a.ws_chunks) * Hq * 2;
+    const float* seq_o = a.ws_o + ((int64_t)seq * a.ws_chunks) * Hq * kD;
+    for (int i = tid; i < Hq * nchunks; i += nt) {
+        const int h = i / nchunks, c = i % nchunks;
+        const float2 ml = __ldcg(reinterpret_cast<const float2*>(seq_ml + ((int64_t)c * Hq + h) * 2));
+        W[i] = ml.x;
+        Lc[i] = ml.y;
+    }
+    __syncthreads();
+    for (int h = tid; h < Hq; h += nt) {
+        float M = -INFINITY;
+        for (int c = 0; c < nchunks; ++c) M = fmaxf(M, W[h * nchunks + c]);
+        float Ls = 0.0f;
+        for (int c = 0; c < nchunks; ++c) {
+            const float w = fast_exp2(W[h * nchunks + c] - M);
+            W[h * nchunks + c] = w;
+            Ls += w * Lc[h * nchunks + c];
+        }
+        MLc[h * 2] = M;
+        MLc[h * 2 + 1] = Ls;
+    }
+    __syncthreads();
+    for (int it = tid; it < Hq * kD / 4; it += nt) {
+        const int h = (it * 4) / kD, dd = (it * 4) % kD;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (int c = 0; c < nchunks; ++c) {
+            const float w = W[h * nchunks + c];
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(seq_o + ((int64_t)c * Hq + h) * kD + dd));
+            acc.x = fmaf(w, v.x, acc.x); acc.y = fmaf(w, v.y, acc.y);
+            acc.z = fmaf(w, v.z, acc.z); acc.w = fmaf(w, v.w, acc.w);
+        }
+        const float inv = emit_partial ? 1.0f : 1.0f / MLc[h * 2 + 1];
+        *reinterpret_cast<float4*>(out + h * kD + dd) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    }
+    if (emit_partial)
+        for (int h = tid; h < Hq; h += nt) {
+            a.partial_ml[((int64_t)seq * Hq + h) * 2] = MLc[h * 2];
+            a.partial_ml[((int64_t)seq * Hq + h) * 2 + 1] = MLc[h * 2 + 1];
+        }
+    if (tid == 0) a.ws_cnt[seq] = 0u;  // leave the ticket zeroed for the next call
+}
+
 // GT: unroll bound for the query heads of one KV head (the actual count a.G <= GT).
 template <int KT, int VT, int GT>
 __global__ void __launch_bounds__(kThreads) decode_kernel(const Args a) {
@@ -445,39 +498,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const Args a) {
     __syncthreads();
     if (!*flag) return;
     __threadfence();
-    float* W = reinterpret_cast<float*>(smem + L.pd);  // [Hq][nchunks] weights, then [Hq][2] (M, L)
-    float* MLc = W + Hq * nchunks;
-    const float* seq_ml = a.ws_ml + ((int64_t)seq * a.ws_chunks) * Hq * 2;
-    const float* seq_o = a.ws_o + ((int64_t)seq * a.ws_chunks) * Hq * kD;
-    for (int h = tid; h < Hq; h += kThreads) {
-        float M = -INFINITY;
-        for (int c = 0; c < nchunks; ++c) M = fmaxf(M, __ldcg(seq_ml + ((int64_t)c * Hq + h) * 2));
-        float Ls = 0.0f;
-        for (int c = 0; c < nchunks; ++c) {
-            const float w = fast_exp2(__ldcg(seq_ml + ((int64_t)c * Hq + h) * 2) - M);
-            W[h * nchunks + c] = w;
-            Ls += w * __ldcg(seq_ml + ((int64_t)c * Hq + h) * 2 + 1);
-        }
-        MLc[h * 2] = M;
-        MLc[h * 2 + 1] = Ls;
-    }
-    __syncthreads();
-    for (int it = tid; it < Hq * kD; it += kThreads) {
-        const int h = it / kD, dd = it % kD;
-        float acc = 0.0f;
-        for (int c = 0; c < nchunks; ++c) acc = fmaf(W[h * nchunks + c], __ldcg(seq_o + ((int64_t)c * Hq + h) * kD + dd), acc);
-        if (emit_partial) {
-            out[h * kD + dd] = acc;
-        } else {
-            out[h * kD + dd] = acc / MLc[h * 2 + 1];
-        }
-    }
-    if (emit_partial)
-        for (int h = tid; h < Hq; h += kThreads) {
-            a.partial_ml[((int64_t)seq * Hq + h) * 2] = MLc[h * 2];
-            a.partial_ml[((int64_t)seq * Hq + h) * 2 + 1] = MLc[h * 2 + 1];
-        }
-    if (tid == 0) a.ws_cnt[seq] = 0u;  // leave the ticket zeroed for the next call
+    combine_chunks(a, seq, nchunks, out, reinterpret_cast<float*>(smem + L.pd));
 }
 
 }  // namespace dec

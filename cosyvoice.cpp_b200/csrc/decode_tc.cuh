@@ -323,7 +323,9 @@ __global__ void __launch_bounds__(kThreads, 2) decode_tc_kernel(const Args a) {
                     make_uint4(w[4 * c4], w[4 * c4 + 1], w[4 * c4 + 2], w[4 * c4 + 3]);
             dv[(g * 2 + blk) * kC + key] = d;
             if constexpr (V_MIN) mv[(g * 2 + blk) * kC + key] = m;
-            atomicMax(&vsc[g * 2 + blk], __float_as_uint(fabsf(d)));
+            // a warp covers 32 keys of one (g, blk): reduce, then one atomic per warp
+            const float dmax = dec::warp_max(fabsf(d));
+            if (lane == 0) atomicMax(&vsc[g * 2 + blk], __float_as_uint(dmax));
         }
     }
     fence_proxy_async_smem();
@@ -500,36 +502,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_tc_kernel(const Args a) {
             __syncthreads();
             if (*flag) {
                 __threadfence();
-                float* W = reinterpret_cast<float*>(ktile);  // free: the MMAs are done
-                float* MLc = W + Hq * nchunks;
-                const float* seq_ml = a.ws_ml + ((int64_t)seq * a.ws_chunks) * Hq * 2;
-                const float* seq_o = a.ws_o + ((int64_t)seq * a.ws_chunks) * Hq * kD;
-                for (int h = tid; h < Hq; h += kThreads) {
-                    float M = -INFINITY;
-                    for (int c = 0; c < nchunks; ++c) M = fmaxf(M, __ldcg(seq_ml + ((int64_t)c * Hq + h) * 2));
-                    float Ls = 0.0f;
-                    for (int c = 0; c < nchunks; ++c) {
-                        const float w = fast_exp2(__ldcg(seq_ml + ((int64_t)c * Hq + h) * 2) - M);
-                        W[h * nchunks + c] = w;
-                        Ls += w * __ldcg(seq_ml + ((int64_t)c * Hq + h) * 2 + 1);
-                    }
-                    MLc[h * 2] = M;
-                    MLc[h * 2 + 1] = Ls;
-                }
-                __syncthreads();
-                for (int it = tid; it < Hq * kD; it += kThreads) {
-                    const int h = it / kD, dd = it % kD;
-                    float acc = 0.0f;
-                    for (int c = 0; c < nchunks; ++c)
-                        acc = fmaf(W[h * nchunks + c], __ldcg(seq_o + ((int64_t)c * Hq + h) * kD + dd), acc);
-                    out[h * kD + dd] = emit_partial ? acc : acc / MLc[h * 2 + 1];
-                }
-                if (emit_partial)
-                    for (int h = tid; h < Hq; h += kThreads) {
-                        a.partial_ml[((int64_t)seq * Hq + h) * 2] = MLc[h * 2];
-                        a.partial_ml[((int64_t)seq * Hq + h) * 2 + 1] = MLc[h * 2 + 1];
-                    }
-                if (tid == 0) a.ws_cnt[seq] = 0u;
+                combine_chunks(a, seq, nchunks, out, reinterpret_cast<float*>(ktile));  // K tiles are free now
             }
         }
     }
