@@ -1,6 +1,7 @@
 // decode.cu -- host side of the split-KV decode kernel (decode.cuh) and the
 // standalone log-sum-exp combine used for cross-GPU split-KV partials.
 #include "decode.cuh"
+#include "decode_pipe.cuh"
 #include "decode_tc.cuh"
 #include "internal.h"
 
@@ -78,7 +79,7 @@ cudaError_t launch_decode(cudaStream_t stream, const cvattn_decode_params& p, in
     a.ws_o = reinterpret_cast<float*>(ws + cnt_bytes + ml_bytes);
     a.ws_chunks = chunks;
     a.status = status;
-    // tensor-core path: Qwen2 shape, block-quantized or f16 K/V
+    // tensor-core paths: Qwen2 shape (2 KV heads, D 64), block-quantized or f16 K/V
     if (!(p.flags & CVATTN_DECODE_CUDA_CORES) && Hkv == 2 && p.k.head_dim == kD && a.G <= dtc::kHP &&
         dtc::supported_type(p.k.type) && dtc::supported_type(p.v.type)) {
         const int chunks_tc = (p.max_kv_len + dtc::kC - 1) / dtc::kC;
@@ -86,6 +87,27 @@ cudaError_t launch_decode(cudaStream_t stream, const cvattn_decode_params& p, in
         a.ws_chunks = chunks_tc;
         a.ws_ml = reinterpret_cast<float*>(ws + cnt_bytes);
         a.ws_o = reinterpret_cast<float*>(ws + cnt_bytes + align256((size_t)p.n_seq * chunks_tc * p.n_q_heads * 2 * 4));
+        // persistent pipelined kernel when its ring of stages fits one SM
+        static int num_sms = 0;
+        if (num_sms == 0) {
+            int dev = 0;
+            cudaGetDevice(&dev);
+            cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+        }
+        if (!(p.flags & CVATTN_DECODE_NOT_PERSISTENT) && dpipe::supported_type(p.k.type) &&
+            dpipe::supported_type(p.v.type) && p.n_seq <= dpipe::kMaxSeq &&
+            dpipe::smem_bytes(p.k.type, p.v.type) <= 227 * 1024 && num_sms > 0) {
+            const long items = (long)p.n_seq * (chunks_tc > 0 ? chunks_tc : 1);
+            const dim3 grid_p((unsigned)(items < num_sms ? items : num_sms));
+            switch (p.k.type) {
+            case kQ4_0: return dpipe::launch_for_k<kQ4_0>(stream, a, p.v.type, grid_p);
+            case kQ4_1: return dpipe::launch_for_k<kQ4_1>(stream, a, p.v.type, grid_p);
+            case kQ5_0: return dpipe::launch_for_k<kQ5_0>(stream, a, p.v.type, grid_p);
+            case kQ5_1: return dpipe::launch_for_k<kQ5_1>(stream, a, p.v.type, grid_p);
+            case kQ8_0: return dpipe::launch_for_k<kQ8_0>(stream, a, p.v.type, grid_p);
+            default: break;
+            }
+        }
         const dim3 grid_tc((unsigned)(chunks_tc > 0 ? chunks_tc : 1), (unsigned)p.n_seq);
         switch (p.k.type) {
         case kF16: return dtc::launch_for_k<kF16>(stream, a, p.v.type, grid_tc);

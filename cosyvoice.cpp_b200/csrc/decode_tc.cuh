@@ -95,10 +95,24 @@ __device__ __forceinline__ void convert_group(const uint8_t* g, uint32_t (&w)[16
     } else if constexpr (T == kQ8_0) {
         d = h2f(*reinterpret_cast<const uint16_t*>(g));
         m = 0.0f;
+        // 32-bit loads of the (2-byte aligned) quants; byte pairs never straddle
+        // a word, so one PRMT per pair builds (1024 + b0 ^ 0x80, 1024 + b1 ^ 0x80).
+        const uint8_t* qs = g + 2;
+        const uint32_t* wp = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(qs) & ~uintptr_t(3));
+        if (reinterpret_cast<uintptr_t>(qs) & 2) {  // pair i: high half of word (i+1)/2 when i is even
+            uint32_t x[9];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const uint32_t x = (uint32_t)reinterpret_cast<const uint16_t*>(g + 2)[i] ^ 0x8080u;
-            w[i] = hsub2_u32(magic_pair(x), kF16x2_1152);
+            for (int j = 0; j < 9; ++j) x[j] = wp[j] ^ 0x80808080u;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                w[i] = hsub2_u32(__byte_perm(x[(i + 1) >> 1], 0x6464u, (i & 1) ? 0x5140u : 0x5342u), kF16x2_1152);
+        } else {
+            uint32_t x[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) x[j] = wp[j] ^ 0x80808080u;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                w[i] = hsub2_u32(__byte_perm(x[i >> 1], 0x6464u, (i & 1) ? 0x5342u : 0x5140u), kF16x2_1152);
         }
     } else {
         using B = BlockTraits<T>;

@@ -208,8 +208,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
             for (int c = 0; c < 16; ++c) {
                 float4 v = row_ok ? *reinterpret_cast<const float4*>(qrow + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
-                w[2 * c] = tc::pack_f16x2(v.x, v.y);
-                w[2 * c + 1] = tc::pack_f16x2(v.z, v.w);
+                const float sc = p.scale_log2;  // scores leave the MMA already in log2 units
+                w[2 * c] = tc::pack_f16x2(v.x * sc, v.y * sc);
+                w[2 * c + 1] = tc::pack_f16x2(v.z * sc, v.w * sc);
             }
 #pragma unroll
             for (int c = 0; c < 8; ++c)
@@ -226,25 +227,38 @@ __global__ void __launch_bounds__(kThreads, 2)
         float m_ref = -INFINITY, l = 0.0f;
         // visible score in log2 units, or -inf
         auto score = [&](uint32_t bits, int j) -> float {
-            float s = __uint_as_float(bits) * p.scale_log2;
+            float s = __uint_as_float(bits);
             bool vis = j < p.n_kv && row_ok;
             if (p.mask_mode == CVATTN_MASK_CAUSAL) vis = vis && (j <= p.causal_offset + i);
             else if (p.mask_mode == CVATTN_MASK_CHUNK) vis = vis && (j < p.key_offset || j - p.key_offset < be);
             else if (p.mask_mode == CVATTN_MASK_EXPLICIT && vis) s += h2f(mrow[j]) * 1.4426950408889634f;
             return vis ? s : -INFINITY;
         };
+        // first key index at which some row of this query tile may be masked
+        int full_below = p.n_kv;
+        if (p.mask_mode == CVATTN_MASK_CAUSAL) full_below = min(full_below, p.causal_offset + i0 + 1);
+        else if (p.mask_mode == CVATTN_MASK_CHUNK) {
+            const int be0 = block_end(p, i0 + p.row_offset);
+            full_below = min(full_below, be0 == 0x7fffffff ? p.n_kv : p.key_offset + be0);
+        } else if (p.mask_mode == CVATTN_MASK_EXPLICIT) full_below = 0;
         for (int jt = 0; jt < n_tiles; ++jt) {
             // waits are made warp-uniform: the tcgen05.ld/st below are warp-collective
             if (!__all_sync(0xffffffffu, wait_or_flag(&B->s_full, jt & 1, B, p.status, 1))) break;
             tc::fence_after();
+            const bool full = (jt + 1) * BN <= full_below;
             // pass 1: tile max
             float mt = -INFINITY;
             for (int c = 0; c < 4; ++c) {
                 uint32_t sv[32];
                 tc::tmem_ld32(tmem + lane_base + kSCol + 32 * c, sv);
                 tc::tmem_ld_wait();
+                if (full) {
 #pragma unroll
-                for (int e = 0; e < 32; ++e) mt = fmaxf(mt, score(sv[e], jt * BN + 32 * c + e));
+                    for (int e = 0; e < 32; ++e) mt = fmaxf(mt, __uint_as_float(sv[e]));
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) mt = fmaxf(mt, score(sv[e], jt * BN + 32 * c + e));
+                }
             }
             float alpha = 1.0f;
             if (mt > m_ref + kRescaleThreshold) {
@@ -276,13 +290,26 @@ __global__ void __launch_bounds__(kThreads, 2)
                 tc::tmem_ld32(tmem + lane_base + kSCol + 32 * c, sv);
                 tc::tmem_ld_wait();
                 uint32_t pw[16];
+                if (full) {
+                    const float2 neg_mu = make_float2(-mu, -mu), one = make_float2(1.0f, 1.0f);
+                    float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    const float s0 = score(sv[e], jt * BN + 32 * c + e);
-                    const float s1 = score(sv[e + 1], jt * BN + 32 * c + e + 1);
-                    const float p0 = fast_exp2(s0 - mu), p1 = fast_exp2(s1 - mu);
-                    l += p0 + p1;
-                    pw[e / 2] = tc::pack_f16x2(p0, p1);
+                    for (int e = 0; e < 32; e += 2) {
+                        const float2 x = ffma2(make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), one, neg_mu);
+                        const float2 pp = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+                        acc = ffma2(pp, one, acc);
+                        pw[e / 2] = tc::pack_f16x2(pp.x, pp.y);
+                    }
+                    l += acc.x + acc.y;
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; e += 2) {
+                        const float s0 = score(sv[e], jt * BN + 32 * c + e);
+                        const float s1 = score(sv[e + 1], jt * BN + 32 * c + e + 1);
+                        const float p0 = fast_exp2(s0 - mu), p1 = fast_exp2(s1 - mu);
+                        l += p0 + p1;
+                        pw[e / 2] = tc::pack_f16x2(p0, p1);
+                    }
                 }
                 uint8_t* half = smem + kPOff + (c >> 1) * 16384;
 #pragma unroll

@@ -150,7 +150,8 @@ cvattn_status cvattn_kv_dequantize(cvattn_context* ctx, void* stream, const cvat
 
 enum {
     CVATTN_DECODE_EMIT_PARTIAL = 1,  /* write unnormalized O and (max, sum) instead of O/sum */
-    CVATTN_DECODE_CUDA_CORES = 2     /* use the CUDA-core kernel even where the tensor-core one applies */
+    CVATTN_DECODE_CUDA_CORES = 2,    /* use the CUDA-core kernel even where the tensor-core one applies */
+    CVATTN_DECODE_NOT_PERSISTENT = 4 /* use the one-chunk-per-CTA tensor-core kernel, not the pipelined one */
 };
 
 /* One decode token per sequence: ggml_flash_attn_ext with n_q = 1 and no mask

@@ -55,7 +55,10 @@ def reference(oracle, kt, vt, kq, vq, q, lens):
     return out
 
 
-@pytest.mark.parametrize("path", ["tensor_cores", "cuda_cores"])
+PATHS = {"pipelined": {}, "tensor_cores": {"not_persistent": True}, "cuda_cores": {"cuda_cores": True}}
+
+
+@pytest.mark.parametrize("path", list(PATHS))
 @pytest.mark.parametrize("kname", ALL)
 @pytest.mark.parametrize("vname", ALL)
 def test_decode_type_pairs(ctx, cv, cuda, oracle, kname, vname, path):
@@ -67,13 +70,13 @@ def test_decode_type_pairs(ctx, cv, cuda, oracle, kname, vname, path):
     q = rng.standard_normal((len(lens), HQ, D)).astype(np.float32)
     qt = torch.tensor(q, device="cuda")
     kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
-    out = cv.decode(ctx, qt, kd, vd, kl, max(lens), cuda_cores=(path == "cuda_cores")).cpu().numpy()
+    out = cv.decode(ctx, qt, kd, vd, kl, max(lens), **PATHS[path]).cpu().numpy()
     ref = reference(oracle, kt, vt, kq, vq, q, lens)
     assert rel_l2(out, ref) <= REL_L2, f"{kname}/{vname} {path} rel-L2 {rel_l2(out, ref):.3e}"
     assert np.abs(out - ref).max() <= MAX_ABS
 
 
-@pytest.mark.parametrize("path", ["tensor_cores", "cuda_cores"])
+@pytest.mark.parametrize("path", list(PATHS))
 @pytest.mark.parametrize("kname,vname", [("q8_0", "q8_0"), ("q8_0", "q4_0"), ("q5_1", "q5_1"), ("f16", "f16")])
 def test_decode_mixed_lengths_64_sequences(ctx, cv, cuda, oracle, kname, vname, path):
     """The benchmark mix: 64 sequences, lengths U[128, 2048] (seed 0)."""
@@ -84,15 +87,15 @@ def test_decode_mixed_lengths_64_sequences(ctx, cv, cuda, oracle, kname, vname, 
     kq, vq, kb, vb, kd, vd = build(cv, cuda, oracle, kt, vt, lens, rng, cap=2048)
     q = rng.standard_normal((64, HQ, D)).astype(np.float32)
     kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
-    out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, 2048,
-                    cuda_cores=(path == "cuda_cores")).cpu().numpy()
+    out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, 2048, **PATHS[path]).cpu().numpy()
     ref = reference(oracle, kt, vt, kq, vq, q, lens)
     assert rel_l2(out, ref) <= REL_L2
     assert np.abs(out - ref).max() <= MAX_ABS
 
 
+@pytest.mark.parametrize("path", list(PATHS))
 @pytest.mark.parametrize("kname,vname", [("q8_0", "q8_0"), ("q5_1", "q4_1"), ("f16", "q5_0"), ("f32", "f32")])
-def test_decode_fused_append(ctx, cv, cuda, oracle, kname, vname):
+def test_decode_fused_append(ctx, cv, cuda, oracle, kname, vname, path):
     """The step's K/V row is quantized into the cache at kv_len-1 and attended to."""
     torch = cuda
     kt, vt = cv.TYPE_BY_NAME[kname], cv.TYPE_BY_NAME[vname]
@@ -105,7 +108,7 @@ def test_decode_fused_append(ctx, cv, cuda, oracle, kname, vname):
     vnew = rng.standard_normal((n, HKV * D)).astype(np.float32)
     q = rng.standard_normal((n, HQ, D)).astype(np.float32)
     kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
-    out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, max(lens),
+    out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, max(lens), **PATHS[path],
                     k_new=torch.tensor(knew, device="cuda"), v_new=torch.tensor(vnew, device="cuda")).cpu().numpy()
     kq2, vq2 = kq.copy(), vq.copy()
     for s, L in enumerate(lens):
@@ -221,5 +224,63 @@ def test_decode_tensor_core_scaling_extremes(ctx, cv, cuda, oracle, qscale, vsca
     q = (rng.standard_normal((2, HQ, D)) * qscale).astype(np.float32)
     kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
     out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, cap).cpu().numpy()
+    ref = reference(oracle, kt, vt, kq, vq, q, lens)
+    assert rel_l2(out, ref) <= REL_L2, f"rel-L2 {rel_l2(out, ref):.3e}"
+
+
+@pytest.mark.parametrize("path", ["pipelined", "tensor_cores"])
+@pytest.mark.parametrize("kname,vname", [("q8_0", "q4_0"), ("q5_1", "q5_1")])
+def test_decode_many_chunks_per_sm(ctx, cv, cuda, oracle, kname, vname, path):
+    """Hundreds of sequences: each persistent CTA walks a range of several
+    chunks, so runs merge consecutive chunks, cover whole sequences, and cross
+    CTA boundaries; the combine reads only the written partials."""
+    torch = cuda
+    kt, vt = cv.TYPE_BY_NAME[kname], cv.TYPE_BY_NAME[vname]
+    rng = np.random.default_rng(41)
+    lens = rng.integers(1, 3001, 300).tolist()
+    lens[:4] = [1, 128, 3000, 2999]
+    cap = 3000
+    kq, vq, kb, vb, kd, vd = build(cv, cuda, oracle, kt, vt, lens, rng, cap=cap, outliers=True)
+    q = rng.standard_normal((len(lens), HQ, D)).astype(np.float32)
+    kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, cap, **PATHS[path]).cpu().numpy()
+    ref = reference(oracle, kt, vt, kq, vq, q, lens)
+    assert rel_l2(out, ref) <= REL_L2, f"rel-L2 {rel_l2(out, ref):.3e}"
+    assert np.abs(out - ref).max() <= MAX_ABS
+
+
+def test_decode_many_chunks_emit_partial(ctx, cv, cuda, oracle):
+    """Partials (unnormalized O, max in log2 units, sum) of the merged runs."""
+    torch = cuda
+    kt = vt = cv.Q8_0
+    rng = np.random.default_rng(43)
+    lens = rng.integers(1, 2049, 260).tolist()
+    kq, vq, kb, vb, kd, vd = build(cv, cuda, oracle, kt, vt, lens, rng, cap=2048)
+    q = rng.standard_normal((len(lens), HQ, D)).astype(np.float32)
+    kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    pml = torch.zeros((len(lens), HQ, 2), dtype=torch.float32, device="cuda")
+    out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, 2048, emit_partial=True,
+                    partial_ml=pml).cpu().numpy()
+    ml = pml.cpu().numpy()
+    ref = reference(oracle, kt, vt, kq, vq, q, lens)
+    assert rel_l2(out / ml[:, :, 1:2], ref) <= REL_L2
+    for s in (0, 7, 100):  # the max is the true max score (log2 units)
+        L = lens[s]
+        kdq = oracle.dequantize(kt, kq[s, :L], HKV * D).reshape(L, HKV, D).astype(np.float64)
+        for h in (0, 13):
+            smax = (kdq[:, h // 7, :] @ q[s, h].astype(np.float64)).max() * SCALE / np.log(2.0)
+            assert abs(ml[s, h, 0] - smax) <= 1e-4 * max(1.0, abs(smax))
+
+
+def test_decode_long_sequences_direct_combine(ctx, cv, cuda, oracle):
+    """More than 64 chunks per sequence: the merge streams every chunk slot and skips empty ones."""
+    torch = cuda
+    kt, vt = cv.Q8_0, cv.Q8_0
+    rng = np.random.default_rng(47)
+    lens = [9000, 8999, 129, 7000, 4000, 1] + [8500] * 6  # ~850 chunks: runs of several chunks per CTA half
+    kq, vq, kb, vb, kd, vd = build(cv, cuda, oracle, kt, vt, lens, rng, cap=9000)
+    q = rng.standard_normal((len(lens), HQ, D)).astype(np.float32)
+    kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, 9000).cpu().numpy()
     ref = reference(oracle, kt, vt, kq, vq, q, lens)
     assert rel_l2(out, ref) <= REL_L2, f"rel-L2 {rel_l2(out, ref):.3e}"
