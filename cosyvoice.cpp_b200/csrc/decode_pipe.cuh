@@ -536,7 +536,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_pipe_kernel(const Args a) 
                 if (progressed) {
                     t_idle = 0;
                     spins = 0;
-                } else if ((++spins & 255u) == 0) {  // the clock and the error flag are slow to read: poll them rarely
+                    continue;
+                }
+                // nothing ready: sleep briefly on one of the two pending barriers (alternating), so the
+                // issuer neither burns issue slots of its sub-partition nor reacts late to either stage
+                if ((spins & 1u) == 0 && ns < n_local && ns <= no + 1)
+                    mbar_try_wait_hint(&bars[B_TILE_FULL + (ns & 1)], (ns >> 1) & 1, 100u);
+                else if (no < ns)
+                    mbar_try_wait_hint(&bars[B_P_FULL + (no & 1)], (no >> 1) & 1, 100u);
+                if ((++spins & 63u) == 0) {  // the clock and the error flag are slow to read: poll them rarely
                     if (*err) break;
                     const uint64_t now = global_timer_ns();
                     if (t_idle == 0) {
