@@ -1,0 +1,552 @@
+// flash_pipe.cuh -- persistent tcgen05 flash attention with two query tiles
+// per CTA for the multi-query paths: Qwen2 causal prefill
+// (src/cosyvoice-llm.cpp:62 with the mask of :20-29 / :101-108) and DiT
+// attention, cached (src/cosyvoice-graph.cpp:363-366) or uncached (:373-377),
+// with the streaming chunk mask of src/cosyvoice-token2wav.cpp:285-298 and an
+// explicit f16 mask.  Same semantics, parameters and numerics as
+// flash_tc.cuh (ggml_flash_attn_ext, scale 1/sqrt(D), f16 operands, fp32
+// accumulation, softmax statistics and output).
+//
+// One CTA per SM walks work items.  An item is a pair of 128-row query tiles
+// that read the same K/V: two query heads of one KV group (G >= 2), or two
+// consecutive query tiles of one head (G = 1).  Every K/V tile is loaded once
+// for both.
+//   warps 0-3   softmax group 0 (query tile 0), thread = row = TMEM lane
+//   warps 4-7   softmax group 1 (query tile 1)
+//   warps 8-11  producer: K/V tiles of any ggml type -> f16 128B-swizzled
+//               shared memory (3 stages); an f16 cache uses TMA tensor loads
+//   warp 12     MMA issuer: S_x = Q_x K^T into TMEM (M128 N128 K64); P_x is
+//               written to TMEM by its softmax group as f16 and feeds
+//               O_x += P_x V directly from TMEM (M128 N64 K128)
+// TMEM (512 columns): S_0 [0,128) S_1 [128,256) P_0 [256,320) P_1 [320,384)
+// O_0 [384,448) O_1 [448,512).  The issue order S_0(j+1) right after O_0(j)
+// lets each softmax group work on tile j+1 while the tensor core serves the
+// other group.  The softmax keeps a reference max per row and rescales O in
+// TMEM only when a tile raises it by more than 2^8 (so P <= 256 stays exact
+// in f16).  Fully masked key tiles are never loaded.
+#pragma once
+
+#include "flash_tc.cuh"
+
+namespace cvattn {
+namespace fp {
+
+using fa::BM;
+using fa::BN;
+using fa::D;
+using fa::Params;
+
+constexpr int kStages = 3;
+constexpr int kThreads = 416;
+constexpr int kProdWarp0 = 8;
+constexpr int kMmaWarp = 12;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kSCol = 0, kPCol = 256, kOCol = 384;
+constexpr float kRescaleThreshold = 8.0f;
+#ifndef CVATTN_FLASH_EXP_POLY
+#define CVATTN_FLASH_EXP_POLY 0
+#endif
+constexpr bool kExpPoly = CVATTN_FLASH_EXP_POLY != 0;  // part of the exponentials on the FMA pipe
+
+// shared memory (offsets from a 1024-aligned base)
+constexpr int kQOff = 0;                          // 2 x 16 KB
+constexpr int kKOff = 32 * 1024;                  // kStages x 16 KB
+constexpr int kVOff = kKOff + kStages * 16384;    // kStages x 16 KB
+constexpr int kBarOff = kVOff + kStages * 16384;  // 128 KB
+constexpr int kSmemBytes = kBarOff + 256;         // one CTA per SM (TMEM: 512 columns)
+
+struct Bars {
+    uint64_t kv_full[kStages];
+    uint64_t kv_empty[kStages];
+    uint64_t q_full[2];
+    uint64_t s_full[2];
+    uint64_t p_ready[2];
+    uint64_t o_done[2];
+    uint64_t o_free[2];
+    uint32_t tmem_base;
+    int err;
+};
+
+// Bounded wait shared by the roles: gives up after kWaitBudgetNs or once another
+// role has flagged an error, so every thread reaches teardown.
+__device__ __forceinline__ bool wait_or_err(uint64_t* bar, uint32_t parity, int* err, int* status, int site) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+        if (mbar_try_wait_hint(bar, parity, 1000u)) return true;
+        if (*reinterpret_cast<volatile int*>(err)) return false;
+        if (global_timer_ns() - t0 > kWaitBudgetNs) {
+            record_status(status, kStatusTimeout | (site << 8));
+            *reinterpret_cast<volatile int*>(err) = 1;
+            return false;
+        }
+    }
+}
+
+// A work item: batch entry, KV head, and per query tile x its head and row
+// tile (active[x] = 0 when the pair has only one tile).
+struct Item {
+    int b, g;
+    int h[2], qt[2];
+    bool active[2];
+};
+
+// Items are ordered longest first (query tile index descending) so the
+// causal / chunk-masked tail finishes together.
+__device__ __forceinline__ Item item_at(const Params& p, int idx) {
+    Item it;
+    const int n_qt = (p.n_q + BM - 1) / BM;
+    const int Hkv = p.Hq / p.G;
+    if (p.G >= 2) {
+        const int pairs = (p.G + 1) / 2;
+        const int per_qt = p.batch * Hkv * pairs;
+        const int qt = n_qt - 1 - idx / per_qt;
+        int r = idx % per_qt;
+        const int pi = r % pairs; r /= pairs;
+        it.g = r % Hkv;
+        it.b = r / Hkv;
+        it.h[0] = it.g * p.G + 2 * pi;
+        it.h[1] = it.h[0] + 1;
+        it.active[0] = true;
+        it.active[1] = 2 * pi + 1 < p.G;
+        it.qt[0] = it.qt[1] = qt;
+    } else {
+        const int qpairs = (n_qt + 1) / 2;
+        const int per_qp = p.batch * p.Hq;
+        const int qp = qpairs - 1 - idx / per_qp;
+        const int r = idx % per_qp;
+        it.h[0] = it.h[1] = r % p.Hq;
+        it.g = it.h[0];
+        it.b = r / p.Hq;
+        it.qt[0] = 2 * qp;
+        it.qt[1] = 2 * qp + 1;
+        it.active[0] = true;
+        it.active[1] = it.qt[1] < n_qt;
+    }
+    return it;
+}
+
+__device__ __forceinline__ int n_items(const Params& p) {
+    const int n_qt = (p.n_q + BM - 1) / BM;
+    const int Hkv = p.Hq / p.G;
+    if (p.G >= 2) return n_qt * p.batch * Hkv * ((p.G + 1) / 2);
+    return ((n_qt + 1) / 2) * p.batch * p.Hq;
+}
+
+// Key tiles query tile qt needs (0 for an inactive tile).
+__device__ __forceinline__ int tiles_of(const Params& p, bool active, int qt) {
+    if (!active) return 0;
+    return (fa::key_limit(p, qt * BM) + BN - 1) / BN;
+}
+
+// 2^x for a pair on the FMA pipe (offloads the MUFU, which caps D = 64
+// attention): Cody-Waite reduction x = n + f with n = round(x) (adding
+// 1.5 * 2^23 rounds to an integer in the low mantissa bits), f in [-1/2, 1/2];
+// 2^f by a degree-4 polynomial fitted here (least squares on the relative
+// error over Chebyshev nodes, Lawson-reweighted toward minimax: max relative
+// error 2.7e-6 in fp32, far below the f16 rounding P receives); 2^n added
+// into the exponent field.  x is clamped to [-126, 127] so the exponent
+// arithmetic stays in range (2^-126 rounds to 0 in f16).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    x.x = fminf(fmaxf(x.x, -126.0f), 127.0f);
+    x.y = fminf(fmaxf(x.y, -126.0f), 127.0f);
+    const float2 one = make_float2(1.0f, 1.0f), magic = make_float2(12582912.0f, 12582912.0f);
+    const float2 t = ffma2(x, one, magic);
+    const float2 r = ffma2(t, one, make_float2(-12582912.0f, -12582912.0f));
+    const float2 f = ffma2(r, make_float2(-1.0f, -1.0f), x);
+    float2 q = make_float2(0.009570101276040077f, 0.009570101276040077f);
+    q = ffma2(q, f, make_float2(0.05591785907745361f, 0.05591785907745361f));
+    q = ffma2(q, f, make_float2(0.240247443318367f, 0.240247443318367f));
+    q = ffma2(q, f, make_float2(0.6931217908859253f, 0.6931217908859253f));
+    q = ffma2(q, f, make_float2(0.9999992847442627f, 0.9999992847442627f));
+    const int n0 = __float_as_int(t.x) - 0x4B400000, n1 = __float_as_int(t.y) - 0x4B400000;
+    return make_float2(__int_as_float(__float_as_int(q.x) + (n0 << 23)), __int_as_float(__float_as_int(q.y) + (n1 << 23)));
+}
+
+// Row max of one S tile (4 x 32 TMEM columns), 4 independent chains.
+template <class Score>
+__device__ __forceinline__ void max_pass(uint32_t s_taddr, bool full, int jt, const Score& score, float& mt) {
+    float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32];
+        tc::tmem_ld32(s_taddr + 32 * c, sv);
+        tc::tmem_ld_wait();
+        if (full) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], __uint_as_float(sv[e]));
+        } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], score(sv[e], jt * BN + 32 * c + e));
+        }
+    }
+    mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+}
+
+// P = 2^(s - mu) of 32 scores (f16 pairs into pw), with running max / sum chains.
+// kPoly: one pair in four is exponentiated on the FMA pipe.
+template <bool kPoly>
+__device__ __forceinline__ void exp_chunk(const float (&sc)[32], float mu, float (&m4)[4], float2 (&acc)[2],
+                                          uint32_t (&pw)[16]) {
+    const float2 neg_mu = make_float2(-mu, -mu), one = make_float2(1.0f, 1.0f);
+#pragma unroll
+    for (int e = 0; e < 32; e += 2) {
+        m4[e & 3] = fmaxf(m4[e & 3], sc[e]);
+        m4[(e + 1) & 3] = fmaxf(m4[(e + 1) & 3], sc[e + 1]);
+        const float2 xx = ffma2(make_float2(sc[e], sc[e + 1]), one, neg_mu);
+        const float2 pp = (kPoly && ((e >> 1) & 3) == 3) ? exp2_poly2(xx) : make_float2(fast_exp2(xx.x), fast_exp2(xx.y));
+        acc[(e >> 1) & 1] = ffma2(pp, one, acc[(e >> 1) & 1]);
+        pw[e / 2] = tc::pack_f16x2(pp.x, pp.y);
+    }
+}
+
+// P = 2^(s - mu) of one S tile into the tile's TMEM P columns, with the tile's
+// row max and sum.  Full tiles (no masked entry in any row) skip the mask.
+template <class Score>
+__device__ __forceinline__ void exp_pass(uint32_t s_taddr, uint32_t p_taddr, bool full, float mu, int jt,
+                                         const Score& score, float& mt, float& lt) {
+    float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+    for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32];
+        tc::tmem_ld32(s_taddr + 32 * c, sv);
+        tc::tmem_ld_wait();
+        float sc[32];
+        uint32_t pw[16];
+        if (full) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) sc[e] = __uint_as_float(sv[e]);
+            exp_chunk<kExpPoly>(sc, mu, m4, acc, pw);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) sc[e] = score(sv[e], jt * BN + 32 * c + e);
+            exp_chunk<false>(sc, mu, m4, acc, pw);
+        }
+        tc::tmem_st16(p_taddr + 16 * c, pw);
+    }
+    mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+    lt = (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y);
+}
+
+template <int KT, int VT>
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_pipe_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap kmap,
+                      const __grid_constant__ CUtensorMap vmap) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    Bars* B = reinterpret_cast<Bars*>(smem + kBarOff);
+    if (smem_addr(smem) & 1023u) {
+        if (threadIdx.x == 0) record_status(p.status, kStatusTimeout);
+        return;
+    }
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int total = n_items(p);
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&B->kv_full[s], p.use_tma ? 1 : 128);
+            mbar_init(&B->kv_empty[s], 1);
+        }
+        for (int x = 0; x < 2; ++x) {
+            mbar_init(&B->q_full[x], 128);
+            mbar_init(&B->s_full[x], 1);
+            mbar_init(&B->p_ready[x], 128);
+            mbar_init(&B->o_done[x], 1);
+            mbar_init(&B->o_free[x], 128);
+        }
+        B->err = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(&B->tmem_base, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tmem = B->tmem_base;
+
+    if (warp < 8) {
+        // ====================================================== softmax group x
+        const int x = warp >> 2;
+        const int r = tid & 127;  // query row in the tile = TMEM lane
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        const uint32_t s_taddr = tmem + lane_base + kSCol + x * 128;
+        const uint32_t p_taddr = tmem + lane_base + kPCol + x * 64;
+        const uint32_t o_taddr = tmem + lane_base + kOCol + x * 64;
+        uint8_t* qtile = smem + kQOff + x * 16384;
+        uint32_t n_s = 0, n_o = 0;  // phases of s_full[x] / o_done[x] consumed
+        bool ok = true;
+        for (int idx = blockIdx.x; ok && idx < total; idx += gridDim.x) {
+            const Item it = item_at(p, idx);
+            // (selects, not it.h[x]: x is not a compile-time index)
+            if (!(x ? it.active[1] : it.active[0])) continue;
+            const int qt = x ? it.qt[1] : it.qt[0];
+            const int nt = tiles_of(p, true, qt);
+            const int h = x ? it.h[1] : it.h[0], b = it.b;
+            const int i0 = qt * BM, i = i0 + r;
+            const bool row_ok = i < p.n_q;
+            if (nt == 0) {  // no visible key for any row of the tile: zero output
+                if (row_ok) {
+                    float* orow = p.out + (((int64_t)b * p.n_q + i) * p.Hq + h) * D;
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) *reinterpret_cast<float4*>(orow + 4 * c) = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+                continue;
+            }
+            {   // Q row -> f16 (scaled into log2 units) swizzled; the previous item's S MMAs are done
+                const float* qrow = p.q + (int64_t)b * p.q_nb_batch + (int64_t)i * p.q_nb_tok + (int64_t)h * p.q_nb_head;
+                uint32_t w[32];
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    const float4 v = row_ok ? *reinterpret_cast<const float4*>(qrow + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    const float sc = p.scale_log2;
+                    w[2 * c] = tc::pack_f16x2(v.x * sc, v.y * sc);
+                    w[2 * c + 1] = tc::pack_f16x2(v.z * sc, v.w * sc);
+                }
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    *reinterpret_cast<uint4*>(qtile + tc::sw128_offset(r, c)) =
+                        make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+                fence_proxy_async_smem();
+                mbar_arrive(&B->q_full[x]);
+            }
+            const int be = (p.mask_mode == CVATTN_MASK_CHUNK) ? fa::block_end(p, i + p.row_offset) : 0;
+            const uint16_t* mrow = (p.mask_mode == CVATTN_MASK_EXPLICIT && row_ok)
+                                       ? p.mask + (int64_t)b * p.mask_nb2 + (int64_t)i * p.mask_nb1
+                                       : nullptr;
+            auto score = [&](uint32_t bits, int j) -> float {
+                float s = __uint_as_float(bits);
+                bool vis = j < p.n_kv && row_ok;
+                if (p.mask_mode == CVATTN_MASK_CAUSAL) vis = vis && (j <= p.causal_offset + i);
+                else if (p.mask_mode == CVATTN_MASK_CHUNK) vis = vis && (j < p.key_offset || j - p.key_offset < be);
+                else if (p.mask_mode == CVATTN_MASK_EXPLICIT && vis) s += h2f(mrow[j]) * 1.4426950408889634f;
+                return vis ? s : -INFINITY;
+            };
+            int full_below = p.n_kv;  // first key at which some row of the tile may be masked
+            if (p.mask_mode == CVATTN_MASK_CAUSAL) full_below = min(full_below, p.causal_offset + i0 + 1);
+            else if (p.mask_mode == CVATTN_MASK_CHUNK) {
+                const int be0 = fa::block_end(p, i0 + p.row_offset);
+                full_below = min(full_below, be0 == 0x7fffffff ? p.n_kv : p.key_offset + be0);
+            } else if (p.mask_mode == CVATTN_MASK_EXPLICIT) full_below = 0;
+            float m_ref = -INFINITY, l = 0.0f;
+            for (int jt = 0; jt < nt; ++jt) {
+                if (!__all_sync(0xffffffffu, wait_or_err(&B->s_full[x], n_s & 1, &B->err, p.status, 1))) {
+                    ok = false;
+                    break;
+                }
+                ++n_s;
+                tc::fence_after();
+                const bool full = (jt + 1) * BN <= full_below;
+                if (jt > 0) {  // O_x(jt-1) (issued before S_x(jt)) has read P_x, and O_x may be rescaled
+                    if (!__all_sync(0xffffffffu, wait_or_err(&B->o_done[x], n_o & 1, &B->err, p.status, 2))) {
+                        ok = false;
+                        break;
+                    }
+                    ++n_o;
+                    tc::fence_after();
+                }
+                // One pass against the running reference max: P = 2^(s - m_ref) and the tile max
+                // together.  Only when the tile raises the max by more than the threshold (and for
+                // a row's first visible tile) is the tile redone against its own max.
+                float mt = -INFINITY;
+                float lt = 0.0f;
+                if (__any_sync(0xffffffffu, m_ref != -INFINITY))
+                    exp_pass(s_taddr, p_taddr, full, m_ref == -INFINITY ? 0.0f : m_ref, jt, score, mt, lt);
+                else
+                    max_pass(s_taddr, full, jt, score, mt);
+                const bool redo = mt > m_ref + kRescaleThreshold;
+                if (__any_sync(0xffffffffu, redo)) {
+                    float alpha = 1.0f;
+                    if (redo) {
+                        alpha = (m_ref == -INFINITY) ? 0.0f : fast_exp2(m_ref - mt);
+                        m_ref = mt;
+                        l *= alpha;
+                    }
+                    if (jt > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+                        for (int c = 0; c < 2; ++c) {
+                            uint32_t ov[32];
+                            tc::tmem_ld32(o_taddr + 32 * c, ov);
+                            tc::tmem_ld_wait();
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+                            tc::tmem_st32(o_taddr + 32 * c, ov);
+                        }
+                    }
+                    float mt2;
+                    lt = 0.0f;
+                    exp_pass(s_taddr, p_taddr, full, m_ref == -INFINITY ? 0.0f : m_ref, jt, score, mt2, lt);
+                }
+                l += lt;
+                tc::tmem_st_wait();
+                tc::fence_before();
+                mbar_arrive(&B->p_ready[x]);
+            }
+            if (!ok) break;
+            // epilogue: O_x(nt-1) complete
+            if (!__all_sync(0xffffffffu, wait_or_err(&B->o_done[x], n_o & 1, &B->err, p.status, 3))) {
+                ok = false;
+                break;
+            }
+            ++n_o;
+            tc::fence_after();
+            float o[64];
+            for (int c = 0; c < 2; ++c) {
+                uint32_t ov[32];
+                tc::tmem_ld32(o_taddr + 32 * c, ov);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 32; ++e) o[32 * c + e] = __uint_as_float(ov[e]);
+            }
+            tc::fence_before();
+            mbar_arrive(&B->o_free[x]);
+            if (row_ok) {
+                const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+                float* orow = p.out + (((int64_t)b * p.n_q + i) * p.Hq + h) * D;
+#pragma unroll
+                for (int c = 0; c < 16; ++c)
+                    *reinterpret_cast<float4*>(orow + 4 * c) =
+                        make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv, o[4 * c + 3] * inv);
+            }
+        }
+    } else if (warp < kMmaWarp) {
+        // ====================================================== producer
+        const int r = tid - kProdWarp0 * 32;  // 0..127 = key row of the tile
+        uint32_t n_kv_tiles = 0;
+        for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
+            const Item it = item_at(p, idx);
+            const int nt = max(tiles_of(p, it.active[0], it.qt[0]), tiles_of(p, it.active[1], it.qt[1]));
+            const int b = it.b, g = it.g;
+            bool ok = true;
+            for (int jt = 0; jt < nt; ++jt, ++n_kv_tiles) {
+                const int s = n_kv_tiles % kStages;
+                const uint32_t use = n_kv_tiles / kStages;
+                if (p.use_tma) {
+                    if (r == 0) {
+                        if (use > 0 && !wait_or_err(&B->kv_empty[s], (use - 1) & 1, &B->err, p.status, 4)) {
+                            ok = false;
+                        } else {
+                            mbar_arrive_expect_tx(&B->kv_full[s], 2 * BN * D * 2);
+                            tc::tma_load_3d(smem + kKOff + s * 16384, &kmap, g * D, jt * BN, b, &B->kv_full[s]);
+                            tc::tma_load_3d(smem + kVOff + s * 16384, &vmap, g * D, jt * BN, b, &B->kv_full[s]);
+                        }
+                    }
+                } else {
+                    if (use > 0 && !wait_or_err(&B->kv_empty[s], (use - 1) & 1, &B->err, p.status, 5)) {
+                        ok = false;
+                    } else {
+                        const uint8_t* kbase = p.k + (int64_t)b * p.k_nb2 + (int64_t)g * p.k_head_bytes;
+                        const uint8_t* vbase = p.v + (int64_t)b * p.v_nb2 + (int64_t)g * p.v_head_bytes;
+                        const int key = jt * BN + r;
+                        const bool valid = key < p.n_kv;
+                        fa::store_row_f16<KT>(kbase + (int64_t)key * p.k_nb1, valid, smem + kKOff + s * 16384, r);
+                        fa::store_row_f16<VT>(vbase + (int64_t)key * p.v_nb1, valid, smem + kVOff + s * 16384, r);
+                        fence_proxy_async_smem();
+                        mbar_arrive(&B->kv_full[s]);
+                    }
+                }
+                if (p.use_tma ? (r == 0 && !ok) : !__all_sync(0xffffffffu, ok)) break;
+            }
+            if (!ok || *reinterpret_cast<volatile int*>(&B->err)) break;
+        }
+    } else if (warp == kMmaWarp && lane == 0) {
+        // ====================================================== MMA issuer
+        const uint32_t idesc_s = tc::idesc_f16_f32(128, 128, false);
+        const uint32_t idesc_o = tc::idesc_f16_f32(128, 64, true);
+        uint32_t n_kv_tiles = 0;
+        uint32_t n_q[2] = {0, 0}, n_p[2] = {0, 0}, n_items_x[2] = {0, 0};
+        bool ok = true;
+        auto issue_s = [&](int x, int stage) {
+            const uint32_t sq = smem_addr(smem + kQOff + x * 16384);
+            const uint32_t kaddr = smem_addr(smem + kKOff + stage * 16384);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+                const uint64_t a = tc::sdesc_sw128(sq + kk * 32, 16, 1024);
+                const uint64_t bb = tc::sdesc_sw128(kaddr + kk * 32, 16, 1024);
+                tc::mma_ss(tmem + kSCol + x * 128, a, bb, idesc_s, kk > 0 ? 1u : 0u);
+            }
+            tc::mma_commit(&B->s_full[x]);
+        };
+        auto issue_o = [&](int x, int stage, bool first) {
+            const uint32_t vaddr = smem_addr(smem + kVOff + stage * 16384);
+#pragma unroll
+            for (int kk = 0; kk < BN / 16; ++kk) {
+                const uint64_t bb = tc::sdesc_sw128(vaddr + kk * 2048, 16, 1024);
+                tc::mma_ts(tmem + kOCol + x * 64, tmem + kPCol + x * 64 + kk * 8, bb, idesc_o, (!first || kk > 0) ? 1u : 0u);
+            }
+            tc::mma_commit(&B->o_done[x]);
+        };
+        for (int idx = blockIdx.x; ok && idx < total; idx += gridDim.x) {
+            const Item it = item_at(p, idx);
+            const int ntx[2] = {tiles_of(p, it.active[0], it.qt[0]), tiles_of(p, it.active[1], it.qt[1])};
+            const int nt = max(ntx[0], ntx[1]);
+            if (nt == 0) continue;
+            // first K/V tile of the item, then S_x(0) for each active tile once its Q is in place
+            ok = wait_or_err(&B->kv_full[n_kv_tiles % kStages], (n_kv_tiles / kStages) & 1, &B->err, p.status, 7);
+#pragma unroll
+            for (int x = 0; x < 2; ++x) {
+                if (!ok) break;
+                if (ntx[x] == 0) continue;
+                ok = wait_or_err(&B->q_full[x], n_q[x] & 1, &B->err, p.status, 6);
+                ++n_q[x];
+                if (!ok) break;
+                tc::fence_after();
+                issue_s(x, n_kv_tiles % kStages);
+            }
+            for (int jt = 0; ok && jt < nt; ++jt) {
+                const uint32_t u = n_kv_tiles + jt;
+                const int s = u % kStages, s_next = (u + 1) % kStages;
+                bool next_loaded = false;
+#pragma unroll
+                for (int x = 0; x < 2; ++x) {
+                    if (!ok) break;
+                    if (jt >= ntx[x]) continue;
+                    // O_x(jt) once P_x(jt) is in TMEM (and, for the item's first O, once the
+                    // previous item's epilogue has read O_x)
+                    ok = wait_or_err(&B->p_ready[x], n_p[x] & 1, &B->err, p.status, 8);
+                    ++n_p[x];
+                    if (ok && jt == 0 && n_items_x[x] > 0)
+                        ok = wait_or_err(&B->o_free[x], (n_items_x[x] - 1) & 1, &B->err, p.status, 9);
+                    if (!ok) break;
+                    tc::fence_after();
+                    issue_o(x, s, jt == 0);
+                    // S_x(jt+1) right behind it, so softmax x overlaps the other tile's O
+                    if (jt + 1 < ntx[x]) {
+                        if (!next_loaded) {
+                            ok = wait_or_err(&B->kv_full[s_next], ((u + 1) / kStages) & 1, &B->err, p.status, 10);
+                            next_loaded = true;
+                            if (!ok) break;
+                            tc::fence_after();
+                        }
+                        issue_s(x, s_next);
+                    }
+                }
+                if (!ok) break;
+                tc::mma_commit(&B->kv_empty[s]);  // stage s is free once everything issued so far completes
+            }
+            n_kv_tiles += nt;
+#pragma unroll
+            for (int x = 0; x < 2; ++x)
+                if (ntx[x] > 0) ++n_items_x[x];
+        }
+    }
+
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after();
+        tc::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+template <int KT>
+cudaError_t launch_for_k(cudaStream_t s, int v_type, const Params& p, const CUtensorMap& km, const CUtensorMap& vm,
+                         dim3 grid);
+template <> cudaError_t launch_for_k<kF32>(cudaStream_t, int, const Params&, const CUtensorMap&, const CUtensorMap&, dim3);
+template <> cudaError_t launch_for_k<kF16>(cudaStream_t, int, const Params&, const CUtensorMap&, const CUtensorMap&, dim3);
+template <> cudaError_t launch_for_k<kQ4_0>(cudaStream_t, int, const Params&, const CUtensorMap&, const CUtensorMap&, dim3);
+template <> cudaError_t launch_for_k<kQ4_1>(cudaStream_t, int, const Params&, const CUtensorMap&, const CUtensorMap&, dim3);
+template <> cudaError_t launch_for_k<kQ5_0>(cudaStream_t, int, const Params&, const CUtensorMap&, const CUtensorMap&, dim3);
+template <> cudaError_t launch_for_k<kQ5_1>(cudaStream_t, int, const Params&, const CUtensorMap&, const CUtensorMap&, dim3);
+template <> cudaError_t launch_for_k<kQ8_0>(cudaStream_t, int, const Params&, const CUtensorMap&, const CUtensorMap&, dim3);
+
+}  // namespace fp
+}  // namespace cvattn

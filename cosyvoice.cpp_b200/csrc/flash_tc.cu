@@ -4,7 +4,7 @@
 
 #include <cstring>
 
-#include "flash_tc.cuh"
+#include "flash_pipe.cuh"
 #include "internal.h"
 
 namespace cvattn {
@@ -70,6 +70,7 @@ cudaError_t launch_flash(cudaStream_t stream, const cvattn_flash_params& a, int*
     p.n_kv = a.n_kv;
     p.Hq = a.n_q_heads;
     p.G = a.n_q_heads / a.k.n_heads;
+    p.batch = a.batch;
     p.scale_log2 = a.scale * 1.4426950408889634f;
     p.mask_mode = a.mask_mode;
     p.mask = a.mask;
@@ -102,6 +103,30 @@ cudaError_t launch_flash(cudaStream_t stream, const cvattn_flash_params& a, int*
         if ((a.v.type == kF16 || a.v.type == kF32) &&
             ((reinterpret_cast<uintptr_t>(a.v.data) & 15) || (a.v.nb1 & 15) || (a.v.nb2 & 15)))
             return cudaErrorInvalidValue;
+    }
+    if (!(a.flags & CVATTN_FLASH_ONE_TILE)) {
+        // persistent kernel: one CTA per SM over the query-tile pairs
+        static int num_sms = 0;
+        if (num_sms == 0) {
+            int dev = 0;
+            cudaGetDevice(&dev);
+            cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+        }
+        const long n_qt = (a.n_q + BM - 1) / BM;
+        const long items = p.G >= 2 ? n_qt * a.batch * (a.n_q_heads / p.G) * ((p.G + 1) / 2)
+                                    : ((n_qt + 1) / 2) * a.batch * a.n_q_heads;
+        if (items <= 0) return cudaSuccess;
+        const dim3 grid_p((unsigned)(items < num_sms ? items : num_sms));
+        switch (a.k.type) {
+        case kF32: return fp::launch_for_k<kF32>(stream, a.v.type, p, km, vm, grid_p);
+        case kF16: return fp::launch_for_k<kF16>(stream, a.v.type, p, km, vm, grid_p);
+        case kQ4_0: return fp::launch_for_k<kQ4_0>(stream, a.v.type, p, km, vm, grid_p);
+        case kQ4_1: return fp::launch_for_k<kQ4_1>(stream, a.v.type, p, km, vm, grid_p);
+        case kQ5_0: return fp::launch_for_k<kQ5_0>(stream, a.v.type, p, km, vm, grid_p);
+        case kQ5_1: return fp::launch_for_k<kQ5_1>(stream, a.v.type, p, km, vm, grid_p);
+        case kQ8_0: return fp::launch_for_k<kQ8_0>(stream, a.v.type, p, km, vm, grid_p);
+        default: return cudaErrorInvalidValue;
+        }
     }
     const dim3 grid((unsigned)((a.n_q + BM - 1) / BM), (unsigned)a.n_q_heads, (unsigned)a.batch);
     switch (a.k.type) {

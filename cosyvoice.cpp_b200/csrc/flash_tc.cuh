@@ -60,7 +60,7 @@ struct Params {
     const uint8_t* v;
     int64_t k_nb1, k_nb2, v_nb1, v_nb2;
     int k_head_bytes, v_head_bytes;
-    int n_q, n_kv, Hq, G;
+    int n_q, n_kv, Hq, G, batch;
     float scale_log2;
     int mask_mode;
     const uint16_t* mask;

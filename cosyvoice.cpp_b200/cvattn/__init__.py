@@ -29,6 +29,7 @@ MASK_NONE, MASK_EXPLICIT, MASK_CAUSAL, MASK_CHUNK = 0, 1, 2, 3
 DECODE_EMIT_PARTIAL = 1
 DECODE_CUDA_CORES = 2
 DECODE_NOT_PERSISTENT = 4
+FLASH_ONE_TILE = 1
 
 OK = 0
 STATUS_NAMES = {0: "OK", 1: "INVALID_ARGUMENT", 2: "UNSUPPORTED", 3: "LENGTH", 4: "ALLOC", 5: "CUDA",
@@ -233,8 +234,9 @@ def combine(partial_o, partial_ml, out=None, stream=None):
 
 def flash_params(q, k: Tensor, v: Tensor, n_kv: int, out, mask_mode: int = MASK_NONE, mask=None,
                  causal_offset: int | None = None, chunk_bounds: Sequence[int] = (), chunk_key_offset: int = 0,
-                 chunk_row_offset: int = 0, scale: float | None = None) -> FlashParams:
-    """q f32 [batch, n_q, Hq, D] (any strides, D contiguous); out f32 [batch, n_q, Hq, D] contiguous."""
+                 chunk_row_offset: int = 0, scale: float | None = None, flags: int = 0) -> FlashParams:
+    """q f32 [batch, n_q, Hq, D] (any strides, D contiguous); out f32 [batch, n_q, Hq, D] contiguous.
+    flags: FLASH_ONE_TILE selects the one-query-tile-per-CTA kernel instead of the persistent one."""
     B, n_q, Hq, D = q.shape
     p = FlashParams()
     p.q = q.data_ptr()
@@ -253,6 +255,7 @@ def flash_params(q, k: Tensor, v: Tensor, n_kv: int, out, mask_mode: int = MASK_
     for i, b in enumerate(chunk_bounds):
         p.chunk_bounds[i] = int(b)
     p.chunk_key_offset, p.chunk_row_offset = chunk_key_offset, chunk_row_offset
+    p.flags = flags
     return p
 
 

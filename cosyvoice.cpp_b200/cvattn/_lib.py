@@ -11,7 +11,7 @@ import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libcvattn.so")
-ABI_VERSION = 1
+ABI_VERSION = 2
 MAX_CHUNK_BOUNDS = 64
 
 c_void_p, c_int32, c_int64, c_uint32, c_float, c_size_t, c_uint8 = (
@@ -44,7 +44,7 @@ class FlashParams(ctypes.Structure):
         ("scale", c_float), ("mask_mode", c_int32), ("mask", c_void_p), ("mask_nb1", c_int64),
         ("mask_nb2", c_int64), ("causal_offset", c_int32), ("n_chunk_bounds", c_int32),
         ("chunk_bounds", c_int32 * MAX_CHUNK_BOUNDS), ("chunk_key_offset", c_int32),
-        ("chunk_row_offset", c_int32),
+        ("chunk_row_offset", c_int32), ("flags", c_int32),
     ]
 
 

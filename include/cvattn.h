@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define CVATTN_ABI_VERSION 1
+#define CVATTN_ABI_VERSION 2
 
 /* ------------------------------------------------------------------ status */
 
@@ -256,7 +256,14 @@ typedef struct cvattn_flash_params {
     int32_t         chunk_bounds[CVATTN_MAX_CHUNK_BOUNDS]; /* ascending chunk ends (host values) */
     int32_t         chunk_key_offset;  /* CHUNK: keys below this are always visible (cached prompt) */
     int32_t         chunk_row_offset;  /* CHUNK: query i uses mask row i + chunk_row_offset */
+    int32_t         flags;             /* CVATTN_FLASH_*; 0 for the default kernel */
 } cvattn_flash_params;
+
+enum {
+    /* one query tile per CTA, shared-memory P (the first tensor-core kernel);
+       the default is the persistent two-tile kernel with P in tensor memory */
+    CVATTN_FLASH_ONE_TILE = 1
+};
 
 cvattn_status cvattn_flash(cvattn_context* ctx, void* stream, const cvattn_flash_params* p);
 

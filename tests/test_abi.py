@@ -40,7 +40,7 @@ def test_every_declared_symbol_is_exported(cvl):
 def test_struct_sizes_match_bindings(cvl):
     for which, st in cvl._lib.STRUCTS.items():
         assert cvl.lib.cvattn_abi_sizeof(which) == ctypes.sizeof(st)
-    assert cvl.lib.cvattn_abi_version() == 1
+    assert cvl.lib.cvattn_abi_version() == cvl._lib.ABI_VERSION == 2
 
 
 def test_row_sizes(cvl):

@@ -43,6 +43,12 @@ def reference(oracle, t_k, t_v, kq, vq, q, n_kv, Hkv, mask=None):
     return out
 
 
+@pytest.fixture(params=["pipelined", "one_tile"])
+def fk(request, cv):
+    """flags of cvattn_flash: the persistent two-tile kernel (default) or the one-tile kernel."""
+    return 0 if request.param == "pipelined" else cv.FLASH_ONE_TILE
+
+
 def check(out, ref, what=""):
     e = np.abs(out - ref).max()
     r = rel_l2(out, ref)
@@ -51,7 +57,7 @@ def check(out, ref, what=""):
 
 @pytest.mark.parametrize("kv_name", ["f16", "q8_0"])
 @pytest.mark.parametrize("n_q,cur", [(1, 0), (37, 0), (128, 0), (256, 0), (300, 45), (256, 700)])
-def test_prefill_causal_qwen2(ctx, cv, cuda, oracle, kv_name, n_q, cur):
+def test_prefill_causal_qwen2(ctx, cv, cuda, oracle, fk, kv_name, n_q, cur):
     torch = cuda
     t = cv.TYPE_BY_NAME[kv_name]
     rng = np.random.default_rng(n_q * 7 + cur)
@@ -60,7 +66,7 @@ def test_prefill_causal_qwen2(ctx, cv, cuda, oracle, kv_name, n_q, cur):
     kq, kb, kd = make_kv(cv, cuda, oracle, t, n_kv, Hkv, B, rng, cap=n_kv + 5)
     vq, vb, vd = make_kv(cv, cuda, oracle, t, n_kv, Hkv, B, rng, cap=n_kv + 5)
     q = rng.standard_normal((B, n_q, Hq, D)).astype(np.float32)
-    out = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, n_kv, mask_mode=cv.MASK_CAUSAL).cpu().numpy()
+    out = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, n_kv, mask_mode=cv.MASK_CAUSAL, flags=fk).cpu().numpy()
     mask = oracle.mask_bits_to_f32(oracle.causal_mask(n_q, n_kv))[None]
     ref = reference(oracle, t, t, kq, vq, q, n_kv, Hkv, mask)
     check(out, ref, f"causal {kv_name} n_q={n_q} cur={cur}")
@@ -68,7 +74,7 @@ def test_prefill_causal_qwen2(ctx, cv, cuda, oracle, kv_name, n_q, cur):
 
 @pytest.mark.parametrize("kname", ALL)
 @pytest.mark.parametrize("vname", ALL)
-def test_flash_type_pairs(ctx, cv, cuda, oracle, kname, vname):
+def test_flash_type_pairs(ctx, cv, cuda, oracle, fk, kname, vname):
     torch = cuda
     kt, vt = cv.TYPE_BY_NAME[kname], cv.TYPE_BY_NAME[vname]
     rng = np.random.default_rng(kt * 31 + vt)
@@ -76,12 +82,12 @@ def test_flash_type_pairs(ctx, cv, cuda, oracle, kname, vname):
     kq, kb, kd = make_kv(cv, cuda, oracle, kt, n_kv, Hkv, B, rng)
     vq, vb, vd = make_kv(cv, cuda, oracle, vt, n_kv, Hkv, B, rng)
     q = rng.standard_normal((B, n_q, Hq, D)).astype(np.float32)
-    out = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, n_kv).cpu().numpy()
+    out = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, n_kv, flags=fk).cpu().numpy()
     check(out, reference(oracle, kt, vt, kq, vq, q, n_kv, Hkv), f"{kname}/{vname}")
 
 
 @pytest.mark.parametrize("S,chunk", [(600, 50), (200, 50), (131, 40)])
-def test_dit_uncached_f32_chunk_mask(ctx, cv, cuda, oracle, S, chunk):
+def test_dit_uncached_f32_chunk_mask(ctx, cv, cuda, oracle, fk, S, chunk):
     """Uncached DiT: f32 K/V activations, H=16 (MHA), CFG batch 2, chunk mask."""
     torch = cuda
     rng = np.random.default_rng(S)
@@ -91,21 +97,21 @@ def test_dit_uncached_f32_chunk_mask(ctx, cv, cuda, oracle, S, chunk):
     q = rng.standard_normal((B, S, H, D)).astype(np.float32)
     bounds = list(range(chunk, S + 1, chunk))
     out = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, S, mask_mode=cv.MASK_CHUNK,
-                   chunk_bounds=bounds).cpu().numpy()
+                   chunk_bounds=bounds, flags=fk).cpu().numpy()
     mask = oracle.mask_bits_to_f32(oracle.chunk_mask(S, bounds))[None]
     check(out, reference(oracle, cv.F32, cv.F32, kq, vq, q, S, H, mask), "dit chunk")
     # the same mask given explicitly (f16 bits, ggml semantics)
     mbits = torch.tensor(oracle.chunk_mask(S, bounds).view(np.int16), device="cuda")
     out2 = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, S, mask_mode=cv.MASK_EXPLICIT,
-                    mask=mbits).cpu().numpy()
+                    mask=mbits, flags=fk).cpu().numpy()
     check(out2, reference(oracle, cv.F32, cv.F32, kq, vq, q, S, H, mask), "dit explicit")
     # unmasked
-    out3 = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, S).cpu().numpy()
+    out3 = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, S, flags=fk).cpu().numpy()
     check(out3, reference(oracle, cv.F32, cv.F32, kq, vq, q, S, H), "dit unmasked")
 
 
 @pytest.mark.parametrize("kname,vname", [("q8_0", "q4_0"), ("f16", "f16"), ("q8_0", "q8_0")])
-def test_dit_cached_prompt_slots(ctx, cv, cuda, oracle, kname, vname):
+def test_dit_cached_prompt_slots(ctx, cv, cuda, oracle, fk, kname, vname):
     """Cached DiT: 300 prompt frames always visible + 600 current frames under
     the chunk mask (the benchmark layout); default DiT KV k=q8_0, v=q4_0
     (src/cosyvoice.cpp:187)."""
@@ -119,13 +125,13 @@ def test_dit_cached_prompt_slots(ctx, cv, cuda, oracle, kname, vname):
     q = rng.standard_normal((B, S, H, D)).astype(np.float32)
     bounds = list(range(50, S + 1, 50))
     out = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, n_kv, mask_mode=cv.MASK_CHUNK,
-                   chunk_bounds=bounds, chunk_key_offset=P).cpu().numpy()
+                   chunk_bounds=bounds, chunk_key_offset=P, flags=fk).cpu().numpy()
     cm = oracle.mask_bits_to_f32(oracle.chunk_mask(S, bounds))
     mask = np.concatenate([np.zeros((S, P), np.float32), cm], axis=1)[None]
     check(out, reference(oracle, kt, vt, kq, vq, q, n_kv, H, mask), f"dit cached {kname}/{vname}")
 
 
-def test_dit_cut_len_queries(ctx, cv, cuda, oracle):
+def test_dit_cut_len_queries(ctx, cv, cuda, oracle, fk):
     """Final DiT block: queries are the last S - cut_len rows (strided view of Q);
     mask rows follow ggml's row order (row i of the mask for query i)."""
     torch = cuda
@@ -138,15 +144,15 @@ def test_dit_cut_len_queries(ctx, cv, cuda, oracle):
     bounds = [100, 200, 260]
     mbits = oracle.chunk_mask(S, bounds)
     out = cv.flash(ctx, qt, kd, vd, S, mask_mode=cv.MASK_EXPLICIT,
-                   mask=torch.tensor(mbits.view(np.int16), device="cuda")).cpu().numpy()
+                   mask=torch.tensor(mbits.view(np.int16), device="cuda"), flags=fk).cpu().numpy()
     mask = oracle.mask_bits_to_f32(mbits)[: S - cut][None]
     check(out, reference(oracle, cv.F32, cv.F32, kq, vq, qfull[:, cut:].copy(), S, H, mask), "cut_len")
     # implicit chunk mask with the same row convention
-    out2 = cv.flash(ctx, qt, kd, vd, S, mask_mode=cv.MASK_CHUNK, chunk_bounds=bounds).cpu().numpy()
+    out2 = cv.flash(ctx, qt, kd, vd, S, mask_mode=cv.MASK_CHUNK, chunk_bounds=bounds, flags=fk).cpu().numpy()
     check(out2, reference(oracle, cv.F32, cv.F32, kq, vq, qfull[:, cut:].copy(), S, H, mask), "cut_len chunk")
 
 
-def test_explicit_random_mask_and_fully_masked_rows(ctx, cv, cuda, oracle):
+def test_explicit_random_mask_and_fully_masked_rows(ctx, cv, cuda, oracle, fk):
     torch = cuda
     rng = np.random.default_rng(99)
     B, Hq, Hkv, n_q, n_kv = 1, 14, 2, 150, 333
@@ -158,16 +164,51 @@ def test_explicit_random_mask_and_fully_masked_rows(ctx, cv, cuda, oracle):
     m[5, :] = -np.inf                      # fully masked row -> zeros
     m[140:, :200] = -np.inf                # first key tiles fully masked for some rows
     out = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, n_kv, mask_mode=cv.MASK_EXPLICIT,
-                   mask=torch.tensor(m.view(np.int16), device="cuda")).cpu().numpy()
+                   mask=torch.tensor(m.view(np.int16), device="cuda"), flags=fk).cpu().numpy()
     ref = reference(oracle, cv.F16, cv.F16, kq, vq, q, n_kv, Hkv, m.astype(np.float32)[None])
     assert not out[0, 5].any()
     check(out, ref, "explicit random mask")
 
 
-def test_empty_kv_gives_zeros(ctx, cv, cuda, oracle):
+def test_empty_kv_gives_zeros(ctx, cv, cuda, oracle, fk):
     torch = cuda
     kb, kd = cv.alloc_kv(cv.Q8_0, 2, 64, 16, 1)
     vb, vd = cv.alloc_kv(cv.Q8_0, 2, 64, 16, 1)
     q = torch.randn(1, 10, 14, 64, device="cuda")
-    out = cv.flash(ctx, q, kd, vd, 0)
+    out = cv.flash(ctx, q, kd, vd, 0, flags=fk)
     assert not out.any()
+
+
+@pytest.mark.parametrize("kv_name", ["f16", "q8_0"])
+def test_prefill_causal_many_items_per_cta(ctx, cv, cuda, oracle, fk, kv_name):
+    """Batch 8 x 1024 causal rows x 14 heads: several work items per persistent
+    CTA (head pairs of one KV group, the odd head alone), longest first."""
+    torch = cuda
+    t = cv.TYPE_BY_NAME[kv_name]
+    rng = np.random.default_rng(5)
+    B, Hq, Hkv, n_q = 8, 14, 2, 1024
+    kq, kb, kd = make_kv(cv, cuda, oracle, t, n_q, Hkv, B, rng)
+    vq, vb, vd = make_kv(cv, cuda, oracle, t, n_q, Hkv, B, rng)
+    q = rng.standard_normal((B, n_q, Hq, D)).astype(np.float32)
+    out = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, n_q, mask_mode=cv.MASK_CAUSAL, flags=fk).cpu().numpy()
+    mask = oracle.mask_bits_to_f32(oracle.causal_mask(n_q, n_q))[None]
+    ref = reference(oracle, t, t, kq, vq, q, n_q, Hkv, mask)
+    check(out, ref, f"causal many items {kv_name}")
+
+
+def test_dit_cached_many_items_per_cta(ctx, cv, cuda, oracle, fk):
+    """DiT layout with 16 batch entries: query-tile pairs of one head share the
+    K/V tiles, the fifth tile of each head runs alone."""
+    torch = cuda
+    rng = np.random.default_rng(6)
+    B, H, P, S = 16, 16, 300, 600
+    n_kv = P + S
+    kq, kb, kd = make_kv(cv, cuda, oracle, cv.F16, n_kv, H, B, rng, cap=1024)
+    vq, vb, vd = make_kv(cv, cuda, oracle, cv.F16, n_kv, H, B, rng, cap=1024)
+    q = rng.standard_normal((B, S, H, D)).astype(np.float32)
+    bounds = list(range(50, S + 1, 50))
+    out = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, n_kv, mask_mode=cv.MASK_CHUNK,
+                   chunk_bounds=bounds, chunk_key_offset=P, flags=fk).cpu().numpy()
+    cm = oracle.mask_bits_to_f32(oracle.chunk_mask(S, bounds))
+    mask = np.concatenate([np.zeros((S, P), np.float32), cm], axis=1)[None]
+    check(out, reference(oracle, cv.F16, cv.F16, kq, vq, q, n_kv, H, mask), "dit cached many items")
