@@ -43,6 +43,7 @@ constexpr int kMmaWarp = 12;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSCol = 0, kPCol = 256, kOCol = 384;
 constexpr float kRescaleThreshold = 8.0f;
+constexpr float kRescaleP = 256.0f;  // 2^kRescaleThreshold
 #ifndef CVATTN_FLASH_EXP_POLY
 #define CVATTN_FLASH_EXP_POLY 0
 #endif
@@ -182,29 +183,32 @@ __device__ __forceinline__ void max_pass(uint32_t s_taddr, bool full, int jt, co
     mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
 }
 
-// P = 2^(s - mu) of 32 scores (f16 pairs into pw), with running max / sum chains.
+// P = 2^(s - mu) of 32 scores (f16 pairs into pw), with the running sum (two
+// chains) and the running f16 max of P (two elementwise maxima per instruction).
 // kPoly: one pair in four is exponentiated on the FMA pipe.
 template <bool kPoly>
-__device__ __forceinline__ void exp_chunk(const float (&sc)[32], float mu, float (&m4)[4], float2 (&acc)[2],
+__device__ __forceinline__ void exp_chunk(const float (&sc)[32], float mu, __half2& pmax, float2 (&acc)[2],
                                           uint32_t (&pw)[16]) {
     const float2 neg_mu = make_float2(-mu, -mu), one = make_float2(1.0f, 1.0f);
 #pragma unroll
     for (int e = 0; e < 32; e += 2) {
-        m4[e & 3] = fmaxf(m4[e & 3], sc[e]);
-        m4[(e + 1) & 3] = fmaxf(m4[(e + 1) & 3], sc[e + 1]);
         const float2 xx = ffma2(make_float2(sc[e], sc[e + 1]), one, neg_mu);
         const float2 pp = (kPoly && ((e >> 1) & 3) == 3) ? exp2_poly2(xx) : make_float2(fast_exp2(xx.x), fast_exp2(xx.y));
         acc[(e >> 1) & 1] = ffma2(pp, one, acc[(e >> 1) & 1]);
         pw[e / 2] = tc::pack_f16x2(pp.x, pp.y);
+        pmax = __hmax2(pmax, *reinterpret_cast<const __half2*>(&pw[e / 2]));
     }
 }
 
 // P = 2^(s - mu) of one S tile into the tile's TMEM P columns, with the tile's
-// row max and sum.  Full tiles (no masked entry in any row) skip the mask.
+// row sum and the largest P of the row (as f16; +inf when P overflowed f16).
+// Full tiles (no masked entry in any row) skip the mask.  (Double-buffering
+// the four TMEM loads measured slower: the larger unrolled body costs more
+// than the load latency it hides.)
 template <class Score>
 __device__ __forceinline__ void exp_pass(uint32_t s_taddr, uint32_t p_taddr, bool full, float mu, int jt,
-                                         const Score& score, float& mt, float& lt) {
-    float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                                         const Score& score, float& pm, float& lt) {
+    __half2 pmax = __float2half2_rn(0.0f);
     float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
     for (int c = 0; c < 4; ++c) {
         uint32_t sv[32];
@@ -215,15 +219,15 @@ __device__ __forceinline__ void exp_pass(uint32_t s_taddr, uint32_t p_taddr, boo
         if (full) {
 #pragma unroll
             for (int e = 0; e < 32; ++e) sc[e] = __uint_as_float(sv[e]);
-            exp_chunk<kExpPoly>(sc, mu, m4, acc, pw);
+            exp_chunk<kExpPoly>(sc, mu, pmax, acc, pw);
         } else {
 #pragma unroll
             for (int e = 0; e < 32; ++e) sc[e] = score(sv[e], jt * BN + 32 * c + e);
-            exp_chunk<false>(sc, mu, m4, acc, pw);
+            exp_chunk<false>(sc, mu, pmax, acc, pw);
         }
         tc::tmem_st16(p_taddr + 16 * c, pw);
     }
-    mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+    pm = fmaxf(__low2float(pmax), __high2float(pmax));
     lt = (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y);
 }
 
@@ -344,19 +348,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ++n_o;
                     tc::fence_after();
                 }
-                // One pass against the running reference max: P = 2^(s - m_ref) and the tile max
-                // together.  Only when the tile raises the max by more than the threshold (and for
-                // a row's first visible tile) is the tile redone against its own max.
-                float mt = -INFINITY;
+                // One pass against the running reference max: P = 2^(s - m_ref), its row sum and
+                // its largest value.  Only when a row's P exceeds 2^threshold (its max rose by more
+                // than the threshold; also a row's first visible tile) is the tile redone against
+                // the tile's own max.
+                float pm = INFINITY;
                 float lt = 0.0f;
                 if (__any_sync(0xffffffffu, m_ref != -INFINITY))
-                    exp_pass(s_taddr, p_taddr, full, m_ref == -INFINITY ? 0.0f : m_ref, jt, score, mt, lt);
-                else
-                    max_pass(s_taddr, full, jt, score, mt);
-                const bool redo = mt > m_ref + kRescaleThreshold;
+                    exp_pass(s_taddr, p_taddr, full, m_ref == -INFINITY ? 0.0f : m_ref, jt, score, pm, lt);
+                const bool redo = m_ref == -INFINITY || !(pm <= kRescaleP);
                 if (__any_sync(0xffffffffu, redo)) {
+                    tc::tmem_st_wait();  // the optimistic P stores land before they are overwritten
+                    float mt = -INFINITY;
+                    max_pass(s_taddr, full, jt, score, mt);
                     float alpha = 1.0f;
-                    if (redo) {
+                    if (mt > m_ref + kRescaleThreshold) {
                         alpha = (m_ref == -INFINITY) ? 0.0f : fast_exp2(m_ref - mt);
                         m_ref = mt;
                         l *= alpha;
@@ -371,9 +377,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tc::tmem_st32(o_taddr + 32 * c, ov);
                         }
                     }
-                    float mt2;
                     lt = 0.0f;
-                    exp_pass(s_taddr, p_taddr, full, m_ref == -INFINITY ? 0.0f : m_ref, jt, score, mt2, lt);
+                    exp_pass(s_taddr, p_taddr, full, m_ref == -INFINITY ? 0.0f : m_ref, jt, score, pm, lt);
                 }
                 l += lt;
                 tc::tmem_st_wait();
