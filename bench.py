@@ -158,8 +158,11 @@ def run_ours(args, rank: int, world: int, torch, dist) -> dict | None:
     row = cv.row_size(kv_type, HKV * D)
     bytes_per_layer = sum(lens) * 2 * row            # K and V rows read by attention
     bytes_per_step = bytes_per_layer * LAYERS
+    # one model step: every layer's fused append + attention; the lengths are
+    # uploaded once and no layer writes another layer's cache, so each launch may
+    # stream its K/V while the previous layer finishes (DECODE_INPUTS_READY)
     decs = [cv.Decoder(ctx, caches[l][1], caches[l][3], N_SEQ, HQ, CAP, q[l], out[l], kv_len,
-                       k_new=k_new[l], v_new=v_new[l]) for l in range(LAYERS)]
+                       k_new=k_new[l], v_new=v_new[l], inputs_ready=True) for l in range(LAYERS)]
     stream = torch.cuda.Stream()
 
     def step(s):

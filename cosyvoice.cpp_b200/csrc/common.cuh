@@ -305,6 +305,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Programmatic dependent launch.  launch_dependents lets the next kernel in the
+// stream (launched with programmatic stream serialization) start its own
+// prologue on SMs this grid frees; wait blocks until every prerequisite grid
+// has completed and its memory is visible (immediately after a kernel that
+// never triggers).  Everything that reads inputs or writes outputs sits behind
+// the wait.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Non-blocking probe of a phase (for issuers that poll several barriers).
 __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
     uint32_t ok;

@@ -400,6 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_pipe_kernel(const Args a) 
     volatile int* flags = reinterpret_cast<volatile int*>(smem + L.misc);
     volatile int* err = reinterpret_cast<volatile int*>(smem + L.misc + 8);
     int* pref = reinterpret_cast<int*>(smem + L.pref);
+    griddep_launch_dependents();  // the next layer's launch may start its prologue on SMs this grid frees
 
     // ---- setup: barriers, TMEM, per-sequence chunk prefix sums
     if (tid == 0) {
@@ -415,18 +416,40 @@ __global__ void __launch_bounds__(kThreads, 1) decode_pipe_kernel(const Args a) 
         tc::tmem_alloc(tmem_slot, kTmemCols);
         tc::tmem_relinquish();
     }
+    // Inputs (Q, new rows, lengths, cache) and the workspace belong to the previous
+    // kernel until griddepcontrol.wait.  With CVATTN_DECODE_INPUTS_READY the lengths
+    // and cached rows are already final: the chunk scan and the producer's K/V
+    // streaming run before the wait; everything that reads Q / new rows or writes
+    // anything waits.
+    const bool early = (a.flags & CVATTN_DECODE_INPUTS_READY) != 0;
+    if (!early) griddep_wait();
     if (warp == 0) {  // exclusive scan of chunk counts; invalid or empty sequences get none
         int carry = 0;
         for (int base = 0; base < n_seq; base += 32) {
             const int s = base + lane;
-            int nc = 0, len = 0;
+            int nc = 0;
             if (s < n_seq) {
-                len = a.kv_len[s];
+                const int len = a.kv_len[s];
                 if (len > 0 && len <= a.capacity && len <= a.max_kv_len) nc = (len + kC - 1) / kC;
             }
-            if (blockIdx.x == 0) {  // block 0 zeroes the outputs of empty / invalid sequences
-                if (s < n_seq && nc == 0 && len != 0) record_status(a.status, kStatusBadLength);
-                uint32_t bad = __ballot_sync(0xffffffffu, s < n_seq && nc == 0);
+            int incl = nc;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            if (s < n_seq) pref[s] = carry + incl - nc;
+            carry += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) pref[n_seq] = carry;
+        if (blockIdx.x == 0) {  // block 0 zeroes the outputs of empty / invalid sequences
+            if (early) griddep_wait();
+            for (int base = 0; base < n_seq; base += 32) {
+                const int s = base + lane;
+                const int len = s < n_seq ? a.kv_len[s] : 0;
+                const bool bad_len = s < n_seq && !(len > 0 && len <= a.capacity && len <= a.max_kv_len);
+                if (bad_len && len != 0) record_status(a.status, kStatusBadLength);
+                uint32_t bad = __ballot_sync(0xffffffffu, bad_len);
                 while (bad) {
                     const int z = base + __ffs(bad) - 1;
                     bad &= bad - 1;
@@ -439,16 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_pipe_kernel(const Args a) 
                         }
                 }
             }
-            int incl = nc;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += y;
-            }
-            if (s < n_seq) pref[s] = carry + incl - nc;
-            carry += __shfl_sync(0xffffffffu, incl, 31);
         }
-        if (lane == 0) pref[n_seq] = carry;
     }
     tc::fence_before();
     __syncthreads();
@@ -559,6 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_pipe_kernel(const Args a) 
         }
     } else if (warp < kSoftWarp0) {
         // ===================================================== converters (group s: items of slot s)
+        if (early) griddep_wait();
         const int s = warp >> 2;
         const int bar_id = kBarConv + s;
         const int key = tid & (kGroup - 1);  // key row of the chunk
@@ -659,6 +674,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_pipe_kernel(const Args a) 
         }
     } else {
         // ===================================================== softmax + epilogue (group s: items of slot s)
+        if (early) griddep_wait();
         const int s = (warp - kSoftWarp0) >> 2;
         const int bar_id = kBarSoft + s;
         const int stid = tid & (kGroup - 1);     // 0..127 = TMEM lane

@@ -15,8 +15,19 @@ static cudaError_t run(cudaStream_t s, const Args& a, dim3 grid) {
     const int smem = smem_bytes(KT, VT);
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    fn<<<grid, kThreads, smem, s>>>(a);
-    return cudaGetLastError();
+    // programmatic stream serialization: the launch may begin while the previous kernel
+    // finishes; the kernel waits (griddepcontrol.wait) before it touches any input
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, fn, a);
 }
 
 template <>

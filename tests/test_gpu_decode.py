@@ -284,3 +284,39 @@ def test_decode_long_sequences_direct_combine(ctx, cv, cuda, oracle):
     out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, 9000).cpu().numpy()
     ref = reference(oracle, kt, vt, kq, vq, q, lens)
     assert rel_l2(out, ref) <= REL_L2, f"rel-L2 {rel_l2(out, ref):.3e}"
+
+
+def test_decode_step_of_layers_inputs_ready(ctx, cv, cuda, oracle):
+    """One model step of several layers launched back to back with the fused
+    append and DECODE_INPUTS_READY (each launch streams its K/V while the
+    previous layer finishes), repeated for two steps: outputs and appended rows
+    match the oracle."""
+    torch = cuda
+    kt = vt = cv.Q8_0
+    rng = np.random.default_rng(53)
+    layers, lens, cap = 4, rng.integers(100, 900, 24).tolist(), 1024
+    n = len(lens)
+    caches = [build(cv, cuda, oracle, kt, vt, lens, rng, cap=cap) for _ in range(layers)]
+    kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    for step in range(2):
+        q = rng.standard_normal((layers, n, HQ, D)).astype(np.float32)
+        knew = rng.standard_normal((layers, n, HKV * D)).astype(np.float32)
+        vnew = rng.standard_normal((layers, n, HKV * D)).astype(np.float32)
+        qt, kt_, vt_ = (torch.tensor(x, device="cuda") for x in (q, knew, vnew))
+        outs = torch.empty_like(qt)
+        decs = [cv.Decoder(ctx, caches[l][4], caches[l][5], n, HQ, cap, qt[l], outs[l], kl, k_new=kt_[l], v_new=vt_[l],
+                           inputs_ready=True) for l in range(layers)]
+        for d in decs:
+            d()
+        got = outs.cpu().numpy()
+        cur = (np.array(lens) + step).tolist()
+        for l in range(layers):
+            kq, vq = caches[l][0], caches[l][1]
+            for s, L in enumerate(cur):
+                kq[s, L - 1] = oracle.quantize(kt, knew[l, s:s + 1])[0]
+                vq[s, L - 1] = oracle.quantize(vt, vnew[l, s:s + 1])[0]
+            ref = reference(oracle, kt, vt, kq, vq, q[l], cur)
+            assert rel_l2(got[l], ref) <= REL_L2, f"step {step} layer {l}: rel-L2 {rel_l2(got[l], ref):.3e}"
+        kl = torch.tensor([L + step + 1 for L in lens], dtype=torch.int32, device="cuda")  # uploaded, as the contract asks
+    for l in range(layers):
+        assert np.array_equal(caches[l][2].view(n, cap, -1).cpu().numpy(), caches[l][0]), "appended K rows"
