@@ -9,21 +9,24 @@
 //
 // One CTA per SM walks work items.  An item is a pair of 128-row query tiles
 // that read the same K/V: two query heads of one KV group (G >= 2), or two
-// consecutive query tiles of one head (G = 1).  Every K/V tile is loaded once
-// for both.
+// consecutive query tiles of one head (G = 1).  Every K/V tile (64 keys) is
+// loaded once for both.
 //   warps 0-3   softmax group 0 (query tile 0), thread = row = TMEM lane
 //   warps 4-7   softmax group 1 (query tile 1)
 //   warps 8-11  producer: K/V tiles of any ggml type -> f16 128B-swizzled
-//               shared memory (3 stages); an f16 cache uses TMA tensor loads
-//   warp 12     MMA issuer: S_x = Q_x K^T into TMEM (M128 N128 K64); P_x is
-//               written to TMEM by its softmax group as f16 and feeds
-//               O_x += P_x V directly from TMEM (M128 N64 K128)
-// TMEM (512 columns): S_0 [0,128) S_1 [128,256) P_0 [256,320) P_1 [320,384)
-// O_0 [384,448) O_1 [448,512).  The issue order S_0(j+1) right after O_0(j)
-// lets each softmax group work on tile j+1 while the tensor core serves the
-// other group.  The softmax keeps a reference max per row and rescales O in
-// TMEM only when a tile raises it by more than 2^8 (so P <= 256 stays exact
-// in f16).  Fully masked key tiles are never loaded.
+//               shared memory (6 stages); an f16 cache uses TMA tensor loads
+//   warps 12-13 MMA issuers, one per query tile x: S_x = Q_x K^T into TMEM
+//               (M128 N64 K64); P_x is written to TMEM by its softmax group as
+//               f16 and feeds O_x += P_x V directly from TMEM (M128 N64 K64).
+//               (One thread issues an MMA in ~30 ns, so the two tiles get an
+//               issuer each.)
+// TMEM (512 columns): per group x two S buffers (64 columns each), two P
+// buffers (32 each) and O (64).  Tile T of a group uses buffer T & 1, so the
+// MMA computes S(T+1) while the softmax works on S(T) and O(T-1) reads the
+// other P buffer: the softmax never waits for an MMA round trip.  The softmax
+// keeps a reference max per row and rescales O in TMEM only when a tile
+// raises it by more than 2^8 (so P <= 256 stays exact in f16).  Fully masked
+// key tiles are never loaded.
 #pragma once
 
 #include "flash_tc.cuh"
@@ -32,16 +35,16 @@ namespace cvattn {
 namespace fp {
 
 using fa::BM;
-using fa::BN;
 using fa::D;
 using fa::Params;
 
-constexpr int kStages = 3;
-constexpr int kThreads = 416;
+constexpr int kBN = 64;  // keys per tile
+constexpr int kStages = 6;
+constexpr int kThreads = 448;
 constexpr int kProdWarp0 = 8;
-constexpr int kMmaWarp = 12;
+constexpr int kMmaWarp = 12;  // warps 12 and 13: MMA issuer of query tile 0 / 1
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kSCol = 0, kPCol = 256, kOCol = 384;
+constexpr uint32_t kSCol = 0, kPCol = 256, kOCol = 384;  // S: x*128 + b*64, P: 256 + x*64 + b*32, O: 384 + x*64
 constexpr float kRescaleThreshold = 8.0f;
 constexpr float kRescaleP = 256.0f;  // 2^kRescaleThreshold
 #ifndef CVATTN_FLASH_EXP_POLY
@@ -50,19 +53,20 @@ constexpr float kRescaleP = 256.0f;  // 2^kRescaleThreshold
 constexpr bool kExpPoly = CVATTN_FLASH_EXP_POLY != 0;  // part of the exponentials on the FMA pipe
 
 // shared memory (offsets from a 1024-aligned base)
-constexpr int kQOff = 0;                          // 2 x 16 KB
-constexpr int kKOff = 32 * 1024;                  // kStages x 16 KB
-constexpr int kVOff = kKOff + kStages * 16384;    // kStages x 16 KB
-constexpr int kBarOff = kVOff + kStages * 16384;  // 128 KB
-constexpr int kSmemBytes = kBarOff + 256;         // one CTA per SM (TMEM: 512 columns)
+constexpr int kTileBytes = kBN * D * 2;              // 8 KB
+constexpr int kQOff = 0;                             // 2 x 16 KB
+constexpr int kKOff = 32 * 1024;                     // kStages x 8 KB
+constexpr int kVOff = kKOff + kStages * kTileBytes;  // kStages x 8 KB
+constexpr int kBarOff = kVOff + kStages * kTileBytes;  // 128 KB
+constexpr int kSmemBytes = kBarOff + 512;            // one CTA per SM (TMEM: 512 columns)
 
 struct Bars {
     uint64_t kv_full[kStages];
     uint64_t kv_empty[kStages];
     uint64_t q_full[2];
-    uint64_t s_full[2];
-    uint64_t p_ready[2];
-    uint64_t o_done[2];
+    uint64_t s_full[2][2];   // [group][buffer]
+    uint64_t p_ready[2][2];
+    uint64_t o_done[2][2];   // O(T) commits o_done[x][T & 1]
     uint64_t o_free[2];
     uint32_t tmem_base;
     int err;
@@ -137,7 +141,7 @@ __device__ __forceinline__ int n_items(const Params& p) {
 // Key tiles query tile qt needs (0 for an inactive tile).
 __device__ __forceinline__ int tiles_of(const Params& p, bool active, int qt) {
     if (!active) return 0;
-    return (fa::key_limit(p, qt * BM) + BN - 1) / BN;
+    return (fa::key_limit(p, qt * BM) + kBN - 1) / kBN;
 }
 
 // 2^x for a pair on the FMA pipe (offloads the MUFU, which caps D = 64
@@ -164,11 +168,11 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
     return make_float2(__int_as_float(__float_as_int(q.x) + (n0 << 23)), __int_as_float(__float_as_int(q.y) + (n1 << 23)));
 }
 
-// Row max of one S tile (4 x 32 TMEM columns), 4 independent chains.
+// Row max of one S tile (64 TMEM columns), 4 independent chains.
 template <class Score>
 __device__ __forceinline__ void max_pass(uint32_t s_taddr, bool full, int jt, const Score& score, float& mt) {
     float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < kBN / 32; ++c) {
         uint32_t sv[32];
         tc::tmem_ld32(s_taddr + 32 * c, sv);
         tc::tmem_ld_wait();
@@ -177,7 +181,7 @@ __device__ __forceinline__ void max_pass(uint32_t s_taddr, bool full, int jt, co
             for (int e = 0; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], __uint_as_float(sv[e]));
         } else {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], score(sv[e], jt * BN + 32 * c + e));
+            for (int e = 0; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], score(sv[e], jt * kBN + 32 * c + e));
         }
     }
     mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
@@ -210,7 +214,7 @@ __device__ __forceinline__ void exp_pass(uint32_t s_taddr, uint32_t p_taddr, boo
                                          const Score& score, float& pm, float& lt) {
     __half2 pmax = __float2half2_rn(0.0f);
     float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < kBN / 32; ++c) {
         uint32_t sv[32];
         tc::tmem_ld32(s_taddr + 32 * c, sv);
         tc::tmem_ld_wait();
@@ -222,7 +226,7 @@ __device__ __forceinline__ void exp_pass(uint32_t s_taddr, uint32_t p_taddr, boo
             exp_chunk<kExpPoly>(sc, mu, pmax, acc, pw);
         } else {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) sc[e] = score(sv[e], jt * BN + 32 * c + e);
+            for (int e = 0; e < 32; ++e) sc[e] = score(sv[e], jt * kBN + 32 * c + e);
             exp_chunk<false>(sc, mu, pmax, acc, pw);
         }
         tc::tmem_st16(p_taddr + 16 * c, pw);
@@ -247,14 +251,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&B->kv_full[s], p.use_tma ? 1 : 128);
-            mbar_init(&B->kv_empty[s], 1);
+            mbar_init(&B->kv_empty[s], 2);  // one arrival per MMA issuer
         }
         for (int x = 0; x < 2; ++x) {
             mbar_init(&B->q_full[x], 128);
-            mbar_init(&B->s_full[x], 1);
-            mbar_init(&B->p_ready[x], 128);
-            mbar_init(&B->o_done[x], 1);
             mbar_init(&B->o_free[x], 128);
+            for (int b = 0; b < 2; ++b) {
+                mbar_init(&B->s_full[x][b], 1);
+                mbar_init(&B->p_ready[x][b], 128);
+                mbar_init(&B->o_done[x][b], 1);
+            }
         }
         B->err = 0;
         fence_mbar_init();
@@ -273,11 +279,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int x = warp >> 2;
         const int r = tid & 127;  // query row in the tile = TMEM lane
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-        const uint32_t s_taddr = tmem + lane_base + kSCol + x * 128;
-        const uint32_t p_taddr = tmem + lane_base + kPCol + x * 64;
+        const uint32_t s_tbase = tmem + lane_base + kSCol + x * 128;  // + buffer * 64
+        const uint32_t p_tbase = tmem + lane_base + kPCol + x * 64;   // + buffer * 32
         const uint32_t o_taddr = tmem + lane_base + kOCol + x * 64;
         uint8_t* qtile = smem + kQOff + x * 16384;
-        uint32_t n_s = 0, n_o = 0;  // phases of s_full[x] / o_done[x] consumed
+        uint32_t T = 0;  // tiles of this group so far (all items): tile T uses buffer T & 1
         bool ok = true;
         for (int idx = blockIdx.x; ok && idx < total; idx += gridDim.x) {
             const Item it = item_at(p, idx);
@@ -332,20 +338,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 full_below = min(full_below, be0 == 0x7fffffff ? p.n_kv : p.key_offset + be0);
             } else if (p.mask_mode == CVATTN_MASK_EXPLICIT) full_below = 0;
             float m_ref = -INFINITY, l = 0.0f;
-            for (int jt = 0; jt < nt; ++jt) {
-                if (!__all_sync(0xffffffffu, wait_or_err(&B->s_full[x], n_s & 1, &B->err, p.status, 1))) {
+            for (int jt = 0; jt < nt; ++jt, ++T) {
+                const int buf = T & 1;
+                const uint32_t s_taddr = s_tbase + buf * 64, p_taddr = p_tbase + buf * 32;
+                if (!__all_sync(0xffffffffu, wait_or_err(&B->s_full[x][buf], (T >> 1) & 1, &B->err, p.status, 1))) {
                     ok = false;
                     break;
                 }
-                ++n_s;
                 tc::fence_after();
-                const bool full = (jt + 1) * BN <= full_below;
-                if (jt > 0) {  // O_x(jt-1) (issued before S_x(jt)) has read P_x, and O_x may be rescaled
-                    if (!__all_sync(0xffffffffu, wait_or_err(&B->o_done[x], n_o & 1, &B->err, p.status, 2))) {
+                const bool full = (jt + 1) * kBN <= full_below;
+                if (T >= 2) {  // P buffer `buf` is free once O(T-2) has read it
+                    if (!__all_sync(0xffffffffu, wait_or_err(&B->o_done[x][buf], ((T - 2) >> 1) & 1, &B->err, p.status, 2))) {
                         ok = false;
                         break;
                     }
-                    ++n_o;
                     tc::fence_after();
                 }
                 // One pass against the running reference max: P = 2^(s - m_ref), its row sum and
@@ -368,6 +374,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         l *= alpha;
                     }
                     if (jt > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+                        // O(T-1) (the other P buffer) accumulates with the old reference first
+                        if (!__all_sync(0xffffffffu, wait_or_err(&B->o_done[x][buf ^ 1], ((T - 1) >> 1) & 1, &B->err, p.status, 11))) {
+                            ok = false;
+                            break;
+                        }
+                        tc::fence_after();
                         for (int c = 0; c < 2; ++c) {
                             uint32_t ov[32];
                             tc::tmem_ld32(o_taddr + 32 * c, ov);
@@ -383,15 +395,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 l += lt;
                 tc::tmem_st_wait();
                 tc::fence_before();
-                mbar_arrive(&B->p_ready[x]);
+                mbar_arrive(&B->p_ready[x][buf]);
             }
             if (!ok) break;
-            // epilogue: O_x(nt-1) complete
-            if (!__all_sync(0xffffffffu, wait_or_err(&B->o_done[x], n_o & 1, &B->err, p.status, 3))) {
+            // epilogue: O_x of the item's last tile (T - 1) complete
+            if (!__all_sync(0xffffffffu, wait_or_err(&B->o_done[x][(T - 1) & 1], ((T - 1) >> 1) & 1, &B->err, p.status, 3))) {
                 ok = false;
                 break;
             }
-            ++n_o;
             tc::fence_after();
             float o[64];
             for (int c = 0; c < 2; ++c) {
@@ -429,9 +440,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (use > 0 && !wait_or_err(&B->kv_empty[s], (use - 1) & 1, &B->err, p.status, 4)) {
                             ok = false;
                         } else {
-                            mbar_arrive_expect_tx(&B->kv_full[s], 2 * BN * D * 2);
-                            tc::tma_load_3d(smem + kKOff + s * 16384, &kmap, g * D, jt * BN, b, &B->kv_full[s]);
-                            tc::tma_load_3d(smem + kVOff + s * 16384, &vmap, g * D, jt * BN, b, &B->kv_full[s]);
+                            mbar_arrive_expect_tx(&B->kv_full[s], 2 * kTileBytes);
+                            tc::tma_load_3d(smem + kKOff + s * kTileBytes, &kmap, g * D, jt * kBN, b, &B->kv_full[s]);
+                            tc::tma_load_3d(smem + kVOff + s * kTileBytes, &vmap, g * D, jt * kBN, b, &B->kv_full[s]);
                         }
                     }
                 } else {
@@ -440,10 +451,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     } else {
                         const uint8_t* kbase = p.k + (int64_t)b * p.k_nb2 + (int64_t)g * p.k_head_bytes;
                         const uint8_t* vbase = p.v + (int64_t)b * p.v_nb2 + (int64_t)g * p.v_head_bytes;
-                        const int key = jt * BN + r;
+                        // threads 0-63 convert the tile's K rows, 64-127 its V rows
+                        const int row = r & (kBN - 1);
+                        const int key = jt * kBN + row;
                         const bool valid = key < p.n_kv;
-                        fa::store_row_f16<KT>(kbase + (int64_t)key * p.k_nb1, valid, smem + kKOff + s * 16384, r);
-                        fa::store_row_f16<VT>(vbase + (int64_t)key * p.v_nb1, valid, smem + kVOff + s * 16384, r);
+                        if (r < kBN) fa::store_row_f16<KT>(kbase + (int64_t)key * p.k_nb1, valid, smem + kKOff + s * kTileBytes, row);
+                        else fa::store_row_f16<VT>(vbase + (int64_t)key * p.v_nb1, valid, smem + kVOff + s * kTileBytes, row);
                         fence_proxy_async_smem();
                         mbar_arrive(&B->kv_full[s]);
                     }
@@ -452,85 +465,91 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (!ok || *reinterpret_cast<volatile int*>(&B->err)) break;
         }
-    } else if (warp == kMmaWarp && lane == 0) {
-        // ====================================================== MMA issuer
-        const uint32_t idesc_s = tc::idesc_f16_f32(128, 128, false);
+    } else if (warp >= kMmaWarp && lane == 0) {
+        // ====================================================== MMA issuer of query tile x
+        const int x = warp - kMmaWarp;
+        const uint32_t idesc_s = tc::idesc_f16_f32(128, kBN, false);
         const uint32_t idesc_o = tc::idesc_f16_f32(128, 64, true);
+        const uint32_t sq = smem_addr(smem + kQOff + x * 16384);
         uint32_t n_kv_tiles = 0;
-        uint32_t n_q[2] = {0, 0}, n_p[2] = {0, 0}, n_items_x[2] = {0, 0};
+        uint32_t Ts = 0, To = 0;  // S / O issued (all items): buffers Ts & 1, To & 1
+        uint32_t n_q = 0, n_items_x = 0;
         bool ok = true;
-        auto issue_s = [&](int x, int stage) {
-            const uint32_t sq = smem_addr(smem + kQOff + x * 16384);
-            const uint32_t kaddr = smem_addr(smem + kKOff + stage * 16384);
+        auto issue_s = [&](int stage) {
+            const uint32_t buf = Ts & 1;
+            const uint32_t kaddr = smem_addr(smem + kKOff + stage * kTileBytes);
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
                 const uint64_t a = tc::sdesc_sw128(sq + kk * 32, 16, 1024);
                 const uint64_t bb = tc::sdesc_sw128(kaddr + kk * 32, 16, 1024);
-                tc::mma_ss(tmem + kSCol + x * 128, a, bb, idesc_s, kk > 0 ? 1u : 0u);
+                tc::mma_ss(tmem + kSCol + x * 128 + buf * 64, a, bb, idesc_s, kk > 0 ? 1u : 0u);
             }
-            tc::mma_commit(&B->s_full[x]);
+            tc::mma_commit(&B->s_full[x][buf]);
+            ++Ts;
         };
-        auto issue_o = [&](int x, int stage, bool first) {
-            const uint32_t vaddr = smem_addr(smem + kVOff + stage * 16384);
+        auto issue_o = [&](int stage, bool first) {
+            const uint32_t buf = To & 1;
+            const uint32_t vaddr = smem_addr(smem + kVOff + stage * kTileBytes);
 #pragma unroll
-            for (int kk = 0; kk < BN / 16; ++kk) {
+            for (int kk = 0; kk < kBN / 16; ++kk) {
                 const uint64_t bb = tc::sdesc_sw128(vaddr + kk * 2048, 16, 1024);
-                tc::mma_ts(tmem + kOCol + x * 64, tmem + kPCol + x * 64 + kk * 8, bb, idesc_o, (!first || kk > 0) ? 1u : 0u);
+                tc::mma_ts(tmem + kOCol + x * 64, tmem + kPCol + x * 64 + buf * 32 + kk * 8, bb, idesc_o,
+                           (!first || kk > 0) ? 1u : 0u);
             }
-            tc::mma_commit(&B->o_done[x]);
+            tc::mma_commit(&B->o_done[x][buf]);
+            ++To;
+        };
+        auto kv_wait = [&](uint32_t u, int site) {
+            const bool r = wait_or_err(&B->kv_full[u % kStages], (u / kStages) & 1, &B->err, p.status, site);
+            if (r) tc::fence_after();
+            return r;
         };
         for (int idx = blockIdx.x; ok && idx < total; idx += gridDim.x) {
             const Item it = item_at(p, idx);
-            const int ntx[2] = {tiles_of(p, it.active[0], it.qt[0]), tiles_of(p, it.active[1], it.qt[1])};
-            const int nt = max(ntx[0], ntx[1]);
-            if (nt == 0) continue;
-            // first K/V tile of the item, then S_x(0) for each active tile once its Q is in place
-            ok = wait_or_err(&B->kv_full[n_kv_tiles % kStages], (n_kv_tiles / kStages) & 1, &B->err, p.status, 7);
-#pragma unroll
-            for (int x = 0; x < 2; ++x) {
-                if (!ok) break;
-                if (ntx[x] == 0) continue;
-                ok = wait_or_err(&B->q_full[x], n_q[x] & 1, &B->err, p.status, 6);
-                ++n_q[x];
-                if (!ok) break;
-                tc::fence_after();
-                issue_s(x, n_kv_tiles % kStages);
+            const int n0 = tiles_of(p, it.active[0], it.qt[0]), n1 = tiles_of(p, it.active[1], it.qt[1]);
+            const int mine = x ? n1 : n0;
+            const int nt = max(n0, n1);
+            const uint32_t base = n_kv_tiles;
+            if (mine > 0) {
+                // S(0), S(1): the two S buffers run ahead of the softmax
+                ok = kv_wait(base, 7) && wait_or_err(&B->q_full[x], n_q & 1, &B->err, p.status, 6);
+                ++n_q;
+                if (ok) {
+                    tc::fence_after();
+                    issue_s((int)(base % kStages));
+                }
+                if (ok && mine > 1) {
+                    ok = kv_wait(base + 1, 10);
+                    if (ok) issue_s((int)((base + 1) % kStages));
+                }
             }
             for (int jt = 0; ok && jt < nt; ++jt) {
-                const uint32_t u = n_kv_tiles + jt;
-                const int s = u % kStages, s_next = (u + 1) % kStages;
-                bool next_loaded = false;
-#pragma unroll
-                for (int x = 0; x < 2; ++x) {
+                const int s = (int)((base + jt) % kStages);
+                if (jt >= mine) {
+                    // this tile's K/V is not read by query tile x; arrive only once the tile has
+                    // landed, so this issuer never arrives twice on a stage in one phase
+                    ok = kv_wait(base + jt, 13);
                     if (!ok) break;
-                    if (jt >= ntx[x]) continue;
-                    // O_x(jt) once P_x(jt) is in TMEM (and, for the item's first O, once the
-                    // previous item's epilogue has read O_x)
-                    ok = wait_or_err(&B->p_ready[x], n_p[x] & 1, &B->err, p.status, 8);
-                    ++n_p[x];
-                    if (ok && jt == 0 && n_items_x[x] > 0)
-                        ok = wait_or_err(&B->o_free[x], (n_items_x[x] - 1) & 1, &B->err, p.status, 9);
-                    if (!ok) break;
-                    tc::fence_after();
-                    issue_o(x, s, jt == 0);
-                    // S_x(jt+1) right behind it, so softmax x overlaps the other tile's O
-                    if (jt + 1 < ntx[x]) {
-                        if (!next_loaded) {
-                            ok = wait_or_err(&B->kv_full[s_next], ((u + 1) / kStages) & 1, &B->err, p.status, 10);
-                            next_loaded = true;
-                            if (!ok) break;
-                            tc::fence_after();
-                        }
-                        issue_s(x, s_next);
-                    }
+                    mbar_arrive(&B->kv_empty[s]);
+                    continue;
                 }
+                // O_x(jt) once P_x(jt) is in TMEM (and, for the item's first O, once the
+                // previous item's epilogue has read O_x)
+                ok = wait_or_err(&B->p_ready[x][To & 1], (To >> 1) & 1, &B->err, p.status, 8);
+                if (ok && jt == 0 && n_items_x > 0)
+                    ok = wait_or_err(&B->o_free[x], (n_items_x - 1) & 1, &B->err, p.status, 9);
                 if (!ok) break;
-                tc::mma_commit(&B->kv_empty[s]);  // stage s is free once everything issued so far completes
+                tc::fence_after();
+                issue_o(s, jt == 0);
+                if (jt + 2 < mine) {  // S_x(jt+2) into the buffer the softmax just released
+                    ok = kv_wait(base + jt + 2, 12);
+                    if (!ok) break;
+                    issue_s((int)((base + jt + 2) % kStages));
+                }
+                tc::mma_commit(&B->kv_empty[s]);  // this issuer is done with stage s once its MMAs complete
             }
             n_kv_tiles += nt;
-#pragma unroll
-            for (int x = 0; x < 2; ++x)
-                if (ntx[x] > 0) ++n_items_x[x];
+            if (mine > 0) ++n_items_x;
         }
     }
 

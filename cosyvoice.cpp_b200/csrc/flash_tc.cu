@@ -29,13 +29,13 @@ static EncodeTiledFn encode_fn() {
 }
 
 // f16 KV tensor as a 3-D map {row elements, n_kv positions, batch}; box of
-// 64 elements x 128 positions, 128B swizzle; positions >= n_kv read as zero.
-static bool make_kv_map(CUtensorMap* map, const cvattn_tensor& t, int n_kv, int batch) {
+// 64 elements x box_rows positions, 128B swizzle; positions >= n_kv read as zero.
+static bool make_kv_map(CUtensorMap* map, const cvattn_tensor& t, int n_kv, int batch, int box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[3] = {(cuuint64_t)t.n_heads * t.head_dim, (cuuint64_t)n_kv, (cuuint64_t)batch};
     const cuuint64_t strides[2] = {(cuuint64_t)t.nb1, (cuuint64_t)t.nb2};
-    const cuuint32_t box[3] = {64, 128, 1};
+    const cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
     const cuuint32_t estride[3] = {1, 1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, t.data, dims, strides, box, estride,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -93,7 +93,9 @@ cudaError_t launch_flash(cudaStream_t stream, const cvattn_flash_params& a, int*
                          ((a.k.nb1 | a.k.nb2 | a.v.nb1 | a.v.nb2) & 15) == 0;
     p.use_tma = 0;
     if (a.k.type == kF16 && a.v.type == kF16 && aligned && a.n_kv > 0) {
-        if (make_kv_map(&km, a.k, a.n_kv, a.batch) && make_kv_map(&vm, a.v, a.n_kv, a.batch)) p.use_tma = 1;
+        // key tiles: 64 keys for the persistent kernel, 128 for the one-tile kernel
+        const int rows = (a.flags & CVATTN_FLASH_ONE_TILE) ? BN : fp::kBN;
+        if (make_kv_map(&km, a.k, a.n_kv, a.batch, rows) && make_kv_map(&vm, a.v, a.n_kv, a.batch, rows)) p.use_tma = 1;
     }
     if (!p.use_tma) {
         // plain-load path reads 16-byte chunks of f16/f32 rows
