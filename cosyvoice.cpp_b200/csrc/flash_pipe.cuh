@@ -97,7 +97,8 @@ struct Item {
 };
 
 // Items are ordered longest first (query tile index descending) so the
-// causal / chunk-masked tail finishes together.
+// causal / chunk-masked tail finishes together; for G = 1 the pairs of one
+// head stay adjacent instead (they read the same K/V).
 __device__ __forceinline__ Item item_at(const Params& p, int idx) {
     Item it;
     const int n_qt = (p.n_q + BM - 1) / BM;
@@ -116,10 +117,11 @@ __device__ __forceinline__ Item item_at(const Params& p, int idx) {
         it.active[1] = 2 * pi + 1 < p.G;
         it.qt[0] = it.qt[1] = qt;
     } else {
+        // the query-tile pairs of one head are neighbours, so the CTAs that run them at
+        // the same time share that head's K/V through L2
         const int qpairs = (n_qt + 1) / 2;
-        const int per_qp = p.batch * p.Hq;
-        const int qp = qpairs - 1 - idx / per_qp;
-        const int r = idx % per_qp;
+        const int qp = qpairs - 1 - idx % qpairs;
+        const int r = idx / qpairs;
         it.h[0] = it.h[1] = r % p.Hq;
         it.g = it.h[0];
         it.b = r / p.Hq;
