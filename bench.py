@@ -292,7 +292,7 @@ def run_ours(args, rank: int, world: int, torch, dist) -> dict | None:
         "e2e": {"value": round(world * bytes_per_step / (e2e_ms_per_step * 1e-3) / 1e9, 1), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms_per_step, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "cvattn_decode via the C ABI; pinned host Q/K/V rows in, outputs back each step"},
-        "roofline": {"bound": "hbm", "kernel": "decode_pipe_kernel<q8_0,q8_0>", "achieved": round(achieved, 1),
+        "roofline": {"bound": "hbm", "kernel": "decode_stream_kernel<q8_0,q8_0>", "achieved": round(achieved, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                      "peak_source": peaks["source"], "launch_us": round(launch_us, 3),
                      "algorithmic_bytes_per_launch": bytes_per_layer, "traffic": traffic},
@@ -302,30 +302,37 @@ def run_ours(args, rank: int, world: int, torch, dist) -> dict | None:
     }
 
 
+def build_cfg4(torch, cv, ctx, kt: int, vt: int, gen):
+    """One configs[3] layer: 256 sequences x 4096 positions of (kt, vt) caches,
+    K/V ~ N(0,1) with 1% of elements at +-8 sigma, appended by the engine."""
+    n, L = 256, 4096
+    pos = torch.arange(L, dtype=torch.int32, device="cuda")
+    kb, kd = cv.alloc_kv(kt, HKV, D, L, n)
+    vb, vd = cv.alloc_kv(vt, HKV, D, L, n)
+    for desc in (kd, vd):
+        x = torch.randn(n, L, HKV * D, device="cuda", generator=gen)
+        hit = torch.rand(x.shape, device="cuda", generator=gen) < 0.01
+        x[hit] = torch.where(torch.rand(int(hit.sum()), device="cuda", generator=gen) < 0.5, -8.0, 8.0)
+        cv.kv_append(ctx, desc, x, pos)
+        del x, hit
+    q = torch.randn(n, HQ, D, device="cuda", generator=gen)
+    out = torch.empty_like(q)
+    kl = torch.full((n,), L, dtype=torch.int32, device="cuda")
+    dec = cv.Decoder(ctx, kd, vd, n, HQ, L, q, out, kl)
+    return dec, (kb, vb, kd, vd, q, out, kl)
+
+
 def run_decode_cfg4(torch, cv, ctx, reps: int = 10) -> dict:
     """asymmetric quantized KV, 256 sequences x 4096 positions, one
     layer per launch (218 / 201 MB of KV: above L2), K/V ~ N(0,1) with 1% of
     elements at +-8 sigma before quantization."""
-    import ctypes
     res = {}
     peaks = measured_peaks()
     n, L = 256, 4096
     gen = torch.Generator(device="cuda")
     gen.manual_seed(77)
-    pos = torch.arange(L, dtype=torch.int32, device="cuda")
     for kt, vt, name in ((cv.Q8_0, cv.Q4_0, "q8_0/q4_0"), (cv.Q5_1, cv.Q5_1, "q5_1/q5_1")):
-        kb, kd = cv.alloc_kv(kt, HKV, D, L, n)
-        vb, vd = cv.alloc_kv(vt, HKV, D, L, n)
-        for desc in (kd, vd):
-            x = torch.randn(n, L, HKV * D, device="cuda", generator=gen)
-            hit = torch.rand(x.shape, device="cuda", generator=gen) < 0.01
-            x[hit] = torch.where(torch.rand(int(hit.sum()), device="cuda", generator=gen) < 0.5, -8.0, 8.0)
-            cv.kv_append(ctx, desc, x, pos)
-            del x, hit
-        q = torch.randn(n, HQ, D, device="cuda", generator=gen)
-        out = torch.empty_like(q)
-        kl = torch.full((n,), L, dtype=torch.int32, device="cuda")
-        dec = cv.Decoder(ctx, kd, vd, n, HQ, L, q, out, kl)
+        dec, keep = build_cfg4(torch, cv, ctx, kt, vt, gen)
         for _ in range(3):
             dec()
         torch.cuda.synchronize()
@@ -342,7 +349,7 @@ def run_decode_cfg4(torch, cv, ctx, reps: int = 10) -> dict:
             "what": f"decode 256 seqs x 4096, {name}, one layer", "gbs": round(gbs, 1), "us_per_launch": round(us, 2),
             "bytes_per_launch": nbytes, "frac_hbm_peak": round(gbs / peaks["hbm_gbs"], 4),
             "peak_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"]}
-        del kb, vb, kd, vd
+        del dec, keep
         torch.cuda.empty_cache()
     st, detail = ctx.sync_status()
     if st != 0:
@@ -495,6 +502,13 @@ def run_profile(args, torch) -> None:
                          k_new=k_new[0], v_new=v_new[0])
         for _ in range(args.steps):
             dec()
+    elif args.profile == "decode_cfg4":
+        # 256 x 4096, q8_0 K / q4_0 V (218 MB)
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(77)
+        dec, keep = build_cfg4(torch, cv, ctx, cv.Q8_0, cv.Q4_0, gen)
+        for _ in range(args.steps):
+            dec()
     else:
         res = run_flash_secondary(torch, cv, ctx, args, only=args.profile, reps=args.steps)
     torch.cuda.synchronize()
@@ -510,7 +524,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-secondary", action="store_true", help="skip the DiT / prefill flash figures")
-    ap.add_argument("--profile", choices=["decode", "dit", "prefill"], default=None,
+    ap.add_argument("--profile", choices=["decode", "decode_cfg4", "dit", "prefill"], default=None,
                     help="only launch the named kernel a few times (for an ncu capture); prints nothing")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

@@ -2,6 +2,7 @@
 // standalone log-sum-exp combine used for cross-GPU split-KV partials.
 #include "decode.cuh"
 #include "decode_pipe.cuh"
+#include "decode_stream.cuh"
 #include "decode_tc.cuh"
 #include "internal.h"
 
@@ -36,8 +37,9 @@ static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 size_t decode_workspace_bytes(int k_type, int v_type, int n_seq, int max_kv_len, int n_q_heads, int n_kv_heads,
                               int head_dim) {
-    const int C = decode_chunk_positions(k_type, v_type, n_kv_heads, head_dim);
+    int C = decode_chunk_positions(k_type, v_type, n_kv_heads, head_dim);
     if (C == 0 || n_seq <= 0 || max_kv_len < 0) return 0;
+    if (C > dstream::kC) C = dstream::kC;  // partial slots for the streaming kernel's 64-position items
     const size_t chunks = (size_t)((max_kv_len + C - 1) / C);
     return align256((size_t)n_seq * 4) + align256((size_t)n_seq * chunks * n_q_heads * 2 * 4) +
            align256((size_t)n_seq * chunks * n_q_heads * kD * 4);
@@ -94,9 +96,31 @@ cudaError_t launch_decode(cudaStream_t stream, const cvattn_decode_params& p, in
             cudaGetDevice(&dev);
             cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
         }
-        if (!(p.flags & CVATTN_DECODE_NOT_PERSISTENT) && dpipe::supported_type(p.k.type) &&
+        const bool persistent = !(p.flags & CVATTN_DECODE_NOT_PERSISTENT) && num_sms > 0;
+        if (persistent && !(p.flags & CVATTN_DECODE_WIDE_CHUNKS) && dstream::supported_type(p.k.type) &&
+            dstream::supported_type(p.v.type) && p.n_seq <= dstream::kMaxSeq &&
+            dstream::smem_bytes(p.k.type, p.v.type) <= 227 * 1024) {
+            // streaming kernel: 64-position items, partial slots per 64 positions
+            const int chunks_s = (p.max_kv_len + dstream::kC - 1) / dstream::kC;
+            Args b = a;
+            b.C = dstream::kC;
+            b.ws_chunks = chunks_s;
+            b.ws_ml = reinterpret_cast<float*>(ws + cnt_bytes);
+            b.ws_o = reinterpret_cast<float*>(ws + cnt_bytes + align256((size_t)p.n_seq * chunks_s * p.n_q_heads * 2 * 4));
+            const long items = (long)p.n_seq * (chunks_s > 0 ? chunks_s : 1);
+            const dim3 grid_s((unsigned)(items < num_sms ? items : num_sms));
+            switch (p.k.type) {
+            case kQ4_0: return dstream::launch_for_k<kQ4_0>(stream, b, p.v.type, grid_s);
+            case kQ4_1: return dstream::launch_for_k<kQ4_1>(stream, b, p.v.type, grid_s);
+            case kQ5_0: return dstream::launch_for_k<kQ5_0>(stream, b, p.v.type, grid_s);
+            case kQ5_1: return dstream::launch_for_k<kQ5_1>(stream, b, p.v.type, grid_s);
+            case kQ8_0: return dstream::launch_for_k<kQ8_0>(stream, b, p.v.type, grid_s);
+            default: break;
+            }
+        }
+        if (persistent && dpipe::supported_type(p.k.type) &&
             dpipe::supported_type(p.v.type) && p.n_seq <= dpipe::kMaxSeq &&
-            dpipe::smem_bytes(p.k.type, p.v.type) <= 227 * 1024 && num_sms > 0) {
+            dpipe::smem_bytes(p.k.type, p.v.type) <= 227 * 1024) {
             const long items = (long)p.n_seq * (chunks_tc > 0 ? chunks_tc : 1);
             const dim3 grid_p((unsigned)(items < num_sms ? items : num_sms));
             switch (p.k.type) {

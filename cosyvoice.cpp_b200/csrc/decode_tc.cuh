@@ -70,9 +70,6 @@ struct Smem {
 
 // ------------------------------------------------- raw group -> f16 exact --
 
-// f16x2 of (1024 + b0, 1024 + b1) for the two low bytes of x.
-__device__ __forceinline__ uint32_t magic_pair(uint32_t x) { return __byte_perm(x, 0x6464u, 0x5140u); }
-
 __device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
     __half2 r = __hsub2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
     return *reinterpret_cast<uint32_t*>(&r);
@@ -84,7 +81,10 @@ constexpr uint32_t kF16x2_1040 = 0x64106410u;  // (1040, 1040)
 constexpr uint32_t kF16x2_1152 = 0x64806480u;  // (1152, 1152)
 
 // 32 elements of one group as exact f16 raw values (w[i] = elements 2i, 2i+1)
-// plus the group's scale and min: element = d * raw + m.
+// plus the group's scale and min: element = d * raw + m.  The raw values are
+// centred (q - 8 for 4-bit, q - 16 for 5-bit quants; q8_0 is signed already)
+// and the min absorbs the offset (m = min + 8 d or min + 16 d), so sums of
+// d * raw over many positions do not cancel against the min term.
 template <int T>
 __device__ __forceinline__ void convert_group(const uint8_t* g, uint32_t (&w)[16], float& d, float& m) {
     if constexpr (T == kF16) {
@@ -117,23 +117,42 @@ __device__ __forceinline__ void convert_group(const uint8_t* g, uint32_t (&w)[16
     } else {
         using B = BlockTraits<T>;
         d = h2f(*reinterpret_cast<const uint16_t*>(g));
-        m = B::HAS_MIN ? h2f(*reinterpret_cast<const uint16_t*>(g + 2)) : 0.0f;
+        constexpr float kCentre = B::OFF_QH >= 0 ? 16.0f : 8.0f;
+        m = B::HAS_MIN ? fmaf(kCentre, d, h2f(*reinterpret_cast<const uint16_t*>(g + 2))) : 0.0f;
         uint32_t qh = 0;
         if constexpr (B::OFF_QH >= 0)
             qh = (uint32_t)*reinterpret_cast<const uint16_t*>(g + B::OFF_QH) |
                  ((uint32_t)*reinterpret_cast<const uint16_t*>(g + B::OFF_QH + 2) << 16);
-        constexpr uint32_t bias = B::HAS_MIN ? kF16x2_1024 : (B::OFF_QH >= 0 ? kF16x2_1040 : kF16x2_1032);
+        constexpr uint32_t bias = B::OFF_QH >= 0 ? kF16x2_1040 : kF16x2_1032;
+        // Quant byte pair p (bytes 2p, 2p+1) spread to [b0, 0, b1, 0]: its low nibbles
+        // are elements 2p, 2p+1, its high nibbles elements 16 + 2p, 17 + 2p.  The
+        // quants start 2-byte aligned, so a pair never straddles a 32-bit word.
+        const uint8_t* qs = g + B::OFF_QS;
+        const uint32_t* wp = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(qs) & ~uintptr_t(3));
+        uint32_t r[8];
+        if (reinterpret_cast<uintptr_t>(qs) & 2) {  // pair p: high half of word (p+1)/2 when p is even
+            uint32_t x[5];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const int j = i & 7;                       // byte pair within the 16 quant bytes
-            const int sh = (i >> 3) << 2;              // elements 16..31 are the high nibbles
-            uint32_t x = ((uint32_t)reinterpret_cast<const uint16_t*>(g + B::OFF_QS)[j] >> sh) & 0x0F0Fu;
-            if constexpr (B::OFF_QH >= 0) {
-                const int e = 2 * i;                   // element index of the low half
-                x |= ((qh >> e) & 1u) << 4;
-                x |= ((qh >> (e + 1)) & 1u) << 12;
+            for (int j = 0; j < 5; ++j) x[j] = wp[j];
+#pragma unroll
+            for (int p = 0; p < 8; ++p) r[p] = __byte_perm(x[(p + 1) >> 1], 0u, (p & 1) ? 0x4140u : 0x4342u);
+        } else {
+            uint32_t x[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) x[j] = wp[j];
+#pragma unroll
+            for (int p = 0; p < 8; ++p) r[p] = __byte_perm(x[p >> 1], 0u, (p & 1) ? 0x4342u : 0x4140u);
+        }
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+            uint32_t lo = (r[p] & 0x000F000Fu) | 0x64006400u;         // (1024 + nibble, 1024 + nibble)
+            uint32_t hi = ((r[p] >> 4) & 0x000F000Fu) | 0x64006400u;
+            if constexpr (B::OFF_QH >= 0) {  // 5th bits: element e takes bit e of qh, at bit 4 / 20 of its pair
+                lo |= (((qh >> (2 * p)) & 3u) * 0x80010u) & 0x00100010u;
+                hi |= (((qh >> (16 + 2 * p)) & 3u) * 0x80010u) & 0x00100010u;
             }
-            w[i] = hsub2_u32(magic_pair(x), bias);
+            w[p] = hsub2_u32(lo, bias);
+            w[8 + p] = hsub2_u32(hi, bias);
         }
     }
 }

@@ -151,7 +151,7 @@ cvattn_status cvattn_kv_dequantize(cvattn_context* ctx, void* stream, const cvat
 enum {
     CVATTN_DECODE_EMIT_PARTIAL = 1,  /* write unnormalized O and (max, sum) instead of O/sum */
     CVATTN_DECODE_CUDA_CORES = 2,    /* use the CUDA-core kernel even where the tensor-core one applies */
-    CVATTN_DECODE_NOT_PERSISTENT = 4, /* use the one-chunk-per-CTA tensor-core kernel, not the pipelined one */
+    CVATTN_DECODE_NOT_PERSISTENT = 4, /* use the one-chunk-per-CTA tensor-core kernel, not a persistent one */
     /* The caller guarantees that kv_len and the cached rows this call reads (all
      * but the row it appends itself) are not written by the kernels just before it
      * on the stream -- e.g. one model step that decodes every layer with the
@@ -159,7 +159,10 @@ enum {
      * starts streaming K/V while the previous kernel is still finishing
      * (programmatic dependent launch); Q, the new rows and all outputs still wait
      * for it. */
-    CVATTN_DECODE_INPUTS_READY = 8
+    CVATTN_DECODE_INPUTS_READY = 8,
+    /* use the persistent kernel with 128-position items and a per-chunk merge
+     * instead of the default streaming one (64-position items, running output) */
+    CVATTN_DECODE_WIDE_CHUNKS = 16
 };
 
 /* One decode token per sequence: ggml_flash_attn_ext with n_q = 1 and no mask

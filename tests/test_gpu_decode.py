@@ -55,7 +55,8 @@ def reference(oracle, kt, vt, kq, vq, q, lens):
     return out
 
 
-PATHS = {"pipelined": {}, "tensor_cores": {"not_persistent": True}, "cuda_cores": {"cuda_cores": True}}
+PATHS = {"streaming": {}, "wide": {"wide_chunks": True}, "tensor_cores": {"not_persistent": True},
+         "cuda_cores": {"cuda_cores": True}}
 
 
 @pytest.mark.parametrize("path", list(PATHS))
@@ -228,7 +229,7 @@ def test_decode_tensor_core_scaling_extremes(ctx, cv, cuda, oracle, qscale, vsca
     assert rel_l2(out, ref) <= REL_L2, f"rel-L2 {rel_l2(out, ref):.3e}"
 
 
-@pytest.mark.parametrize("path", ["pipelined", "tensor_cores"])
+@pytest.mark.parametrize("path", ["streaming", "wide", "tensor_cores"])
 @pytest.mark.parametrize("kname,vname", [("q8_0", "q4_0"), ("q5_1", "q5_1")])
 def test_decode_many_chunks_per_sm(ctx, cv, cuda, oracle, kname, vname, path):
     """Hundreds of sequences: each persistent CTA walks a range of several
@@ -320,3 +321,29 @@ def test_decode_step_of_layers_inputs_ready(ctx, cv, cuda, oracle):
         kl = torch.tensor([L + step + 1 for L in lens], dtype=torch.int32, device="cuda")  # uploaded, as the contract asks
     for l in range(layers):
         assert np.array_equal(caches[l][2].view(n, cap, -1).cpu().numpy(), caches[l][0]), "appended K rows"
+
+
+@pytest.mark.parametrize("path", ["streaming", "wide"])
+@pytest.mark.parametrize("kname,vname", [("q8_0", "q8_0"), ("q4_1", "q5_1")])
+def test_decode_running_rescales(ctx, cv, cuda, oracle, kname, vname, path):
+    """Scores that grow along the sequence and V magnitudes that jump by 2^+-9
+    between 64-position stretches: the streaming kernel's running output is
+    rescaled whenever its reference max or its P' scale has to move."""
+    torch = cuda
+    kt, vt = cv.TYPE_BY_NAME[kname], cv.TYPE_BY_NAME[vname]
+    rng = np.random.default_rng(59)
+    lens = [2000, 1999, 640, 65, 1500, 1]
+    cap, n = 2000, len(lens)
+    pos = np.arange(cap, dtype=np.float32)
+    kx = rng.standard_normal((n, cap, HKV * D)).astype(np.float32) * (0.2 + pos / 400.0)[None, :, None]
+    vx = rng.standard_normal((n, cap, HKV * D)).astype(np.float32)
+    vx *= (2.0 ** rng.integers(-9, 10, (n, cap // 64 + 1)).astype(np.float32)).repeat(64, axis=1)[:, :cap, None]
+    kq, vq = oracle.quantize(kt, kx), oracle.quantize(vt, vx)
+    kd = cv.kv_tensor(torch.tensor(kq.reshape(-1), device="cuda"), kt, HKV, D, cap, n)
+    vd = cv.kv_tensor(torch.tensor(vq.reshape(-1), device="cuda"), vt, HKV, D, cap, n)
+    q = rng.standard_normal((n, HQ, D)).astype(np.float32)
+    kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, cap, **PATHS[path]).cpu().numpy()
+    ref = reference(oracle, kt, vt, kq, vq, q, lens)
+    for s in range(n):
+        assert rel_l2(out[s], ref[s]) <= REL_L2, f"seq {s} rel-L2 {rel_l2(out[s], ref[s]):.3e}"
