@@ -53,7 +53,6 @@ using dec::Args;
 using dtc::convert_group;
 using dtc::pow2f;
 using dpipe::bar_and;
-using dpipe::combine_sparse;
 using dpipe::item_of;
 using dpipe::named_sync;
 using dpipe::pwait;
@@ -174,6 +173,91 @@ __device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t& hi, ui
     const float h1 = __uint_as_float(__float_as_uint(x1) & 0xFFFFE000u);
     hi = tc::pack_f16x2(h0, h1);
     lo = tc::pack_f16x2(x0 - h0, x1 - h1);
+}
+
+// Runs of one sequence: the non-empty intersections of its item range
+// [p_seq, p_seq + nchunks) with the two halves of every CTA's item range (the
+// cut of the main loop).  Each run leaves its partial in the workspace slot of
+// its first chunk; writes those slots to idx and returns their count (at most
+// two per CTA).
+__device__ __forceinline__ int run_slots(int p_seq, int nchunks, int n_items, int grid, int* idx) {
+    const int first = p_seq, end = p_seq + nchunks;
+    // CTA b holds items [b n / grid, (b + 1) n / grid): item i is in CTA ((i + 1) grid - 1) / n
+    const int b0 = (int)(((long long)(first + 1) * grid - 1) / n_items);
+    const int b1 = (int)(((long long)end * grid - 1) / n_items);
+    int r = 0;
+    for (int b = b0; b <= b1; ++b) {
+        const int lo = (int)(((long long)b * n_items) / grid);
+        const int hi = (int)(((long long)(b + 1) * n_items) / grid);
+        const int mid = lo + ((hi - lo + 1) >> 1);
+        const int a0 = max(lo, first), a1 = min(mid, end);
+        if (a0 < a1) idx[r++] = a0 - first;
+        const int c0 = max(mid, first), c1 = min(hi, end);
+        if (c0 < c1) idx[r++] = c0 - first;
+    }
+    return r;
+}
+
+// Log-sum-exp merge of one sequence's run partials by the nt threads of a
+// softmax group: the run slots are known from the cut (no empty slots are
+// read or marked), and each thread = (head, 4 dims) loads the (max, sum) and
+// output of up to 8 runs at once, so a sequence split a few ways takes one
+// round of L2 loads.  idx: dpipe::kRedFloats ints of scratch.
+__device__ __forceinline__ void combine_runs(const Args& a, int seq, int p_seq, int nchunks, int n_items, int grid,
+                                             float* out, int tid, int nt, int bar_id, int* idx) {
+    if (tid == 0) idx[dpipe::kRedFloats - 1] = run_slots(p_seq, nchunks, n_items, grid, idx);
+    named_sync(bar_id, nt);
+    const int R = idx[dpipe::kRedFloats - 1];
+    const int Hq = a.Hq;
+    const bool emit_partial = (a.flags & CVATTN_DECODE_EMIT_PARTIAL) != 0;
+    const float* seq_ml = a.ws_ml + ((int64_t)seq * a.ws_chunks) * Hq * 2;
+    const float* seq_o = a.ws_o + ((int64_t)seq * a.ws_chunks) * Hq * kD;
+    for (int it = tid; it < Hq * (kD / 4); it += nt) {
+        const int h = it / (kD / 4), dd = (it % (kD / 4)) * 4;
+        float M = -INFINITY, Ls = 0.0f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r0 = 0; r0 < R; r0 += 8) {
+            float2 ml[8];
+            float4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int c = idx[min(r0 + j, R - 1)];
+                ml[j] = __ldcg(reinterpret_cast<const float2*>(seq_ml + ((int64_t)c * Hq + h) * 2));
+                v[j] = dpipe::ldcg_f4(seq_o + ((int64_t)c * Hq + h) * kD + dd);
+            }
+            float bm = M;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (r0 + j < R) bm = fmaxf(bm, ml[j].x);
+            const float rs = (M == -INFINITY) ? 0.0f : fast_exp2(M - bm);
+            Ls *= rs;
+            acc.x *= rs; acc.y *= rs; acc.z *= rs; acc.w *= rs;
+            M = bm;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (r0 + j >= R) break;
+                const float w = fast_exp2(ml[j].x - M);
+                Ls = fmaf(w, ml[j].y, Ls);
+                acc.x = fmaf(w, v[j].x, acc.x); acc.y = fmaf(w, v[j].y, acc.y);
+                acc.z = fmaf(w, v[j].z, acc.z); acc.w = fmaf(w, v[j].w, acc.w);
+            }
+        }
+        const float inv = emit_partial ? 1.0f : 1.0f / Ls;
+        *reinterpret_cast<float4*>(out + h * kD + dd) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        if (emit_partial && dd == 0) {
+            a.partial_ml[((int64_t)seq * Hq + h) * 2] = M;
+            a.partial_ml[((int64_t)seq * Hq + h) * 2 + 1] = Ls;
+        }
+    }
+}
+
+// Atomic add with acquire-release semantics at GPU scope: publishes this
+// thread's (and, after a CTA barrier, its group's) earlier writes and sees
+// those of every earlier add on the same counter.
+__device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
 }
 
 // floor(log2(x)) of a positive normal float.
@@ -766,7 +850,7 @@ __global__ void __launch_bounds__(640, 1) decode_stream_kernel(const Args a) {
                     }
                 }
             } else {
-                // partial into the slot of the run's first chunk; the run's other chunk slots are marked empty
+                // partial into the slot of the run's first chunk
                 float* wso = a.ws_o + (((int64_t)seq * a.ws_chunks + run_c0) * Hq) * kD;
                 float* wsml = a.ws_ml + (((int64_t)seq * a.ws_chunks + run_c0) * Hq) * 2;
 #pragma unroll
@@ -776,20 +860,15 @@ __global__ void __launch_bounds__(640, 1) decode_stream_kernel(const Args a) {
                     wso[qh * kD + dim] = run_o[h];
                     if (dim == 0) *reinterpret_cast<float2*>(wsml + qh * 2) = make_float2(mref[h], run_l[h]);
                 }
-                for (int i = stid; i < (run_n - 1) * Hq; i += kGroup) {
-                    float* e = a.ws_ml + (((int64_t)seq * a.ws_chunks + run_c0 + 1 + i / Hq) * Hq + i % Hq) * 2;
-                    *reinterpret_cast<float2*>(e) = make_float2(-INFINITY, 0.0f);
-                }
                 named_sync(bar_id, kGroup);
-                if (stid == 0) {  // the fence after the barrier releases the whole group's writes
-                    __threadfence();
-                    const uint32_t prev = atomicAdd(&a.ws_cnt[seq], (uint32_t)run_n);
+                if (stid == 0) {  // the release after the barrier publishes the whole group's writes
+                    const uint32_t prev = atom_add_acq_rel(&a.ws_cnt[seq], (uint32_t)run_n);
                     flags[s] = (prev + (uint32_t)run_n == (uint32_t)nchunks) ? 1 : 0;
-                    if (flags[s]) __threadfence();
                 }
                 named_sync(bar_id, kGroup);
-                if (flags[s]) {
-                    combine_sparse(a, seq, nchunks, out, stid, kGroup, bar_id, scr);
+                if (flags[s]) {  // the last run to finish merges all of them
+                    combine_runs(a, seq, pref[seq], nchunks, n_items, (int)gridDim.x, out, stid, kGroup, bar_id,
+                                 reinterpret_cast<int*>(scr));
                     if (stid == 0) a.ws_cnt[seq] = 0u;
                 }
             }
