@@ -104,6 +104,7 @@ size_t cvattn_abi_sizeof(int32_t which) {
     case 2: return sizeof(cvattn_flash_params);
     case 3: return sizeof(cvattn_kv_cache_params);
     case 4: return sizeof(cvattn_dit_step);
+    case 5: return sizeof(cvattn_rope_params);
     default: return 0;
     }
 }
@@ -272,6 +273,57 @@ cvattn_status cvattn_kv_append(cvattn_context* ctx, void* stream, const cvattn_t
                                       ctx->status));
 }
 
+// ------------------------------------------------------------------ RoPE
+
+// Validates a RoPE description and forms its device form (theta_scale with the
+// C library's powf, as ggml's CPU backend does).
+static bool rope_dev(const cvattn_rope_params* r, RopeDev& d) {
+    if (!r || (r->mode != CVATTN_ROPE_NORMAL && r->mode != CVATTN_ROPE_NEOX)) return false;
+    if (r->unit_len <= 0 || r->n_dims < 2 || (r->n_dims & 1) || r->n_dims > r->unit_len) return false;
+    if (!(r->freq_base > 0.0f) || !std::isfinite(r->freq_scale) || !std::isfinite(r->attn_factor)) return false;
+    d.mode = r->mode;
+    d.n_dims = r->n_dims;
+    d.unit_len = r->unit_len;
+    d.theta_scale = powf(r->freq_base, -2.0f / (float)r->n_dims);
+    d.freq_scale = r->freq_scale;
+    d.attn_factor = r->attn_factor;
+    return true;
+}
+
+cvattn_status cvattn_rope(void* stream, const cvattn_rope_params* rope, const float* x, int64_t x_nb1, float* out,
+                          int64_t out_nb1, const int32_t* pos, int32_t n_rows, int32_t row_len) {
+    RopeDev d;
+    if (!rope_dev(rope, d) || n_rows < 0 || row_len <= 0 || row_len % rope->unit_len) return CVATTN_ERR_INVALID_ARGUMENT;
+    if (n_rows == 0) return CVATTN_OK;
+    if (!x || !out || !pos || (x_nb1 & 3) || (out_nb1 & 3) || x_nb1 < 4 * (int64_t)row_len ||
+        out_nb1 < 4 * (int64_t)row_len || (reinterpret_cast<uintptr_t>(x) & 3) || (reinterpret_cast<uintptr_t>(out) & 3))
+        return CVATTN_ERR_INVALID_ARGUMENT;
+    if (x == out) {
+        if (x_nb1 != out_nb1) return CVATTN_ERR_INVALID_ARGUMENT;  // in place: same rows
+    } else {
+        // distinct buffers must not overlap
+        const auto* xb = reinterpret_cast<const uint8_t*>(x);
+        const auto* ob = reinterpret_cast<const uint8_t*>(out);
+        if (ob < xb + (int64_t)n_rows * x_nb1 && xb < ob + (int64_t)n_rows * out_nb1) return CVATTN_ERR_INVALID_ARGUMENT;
+    }
+    return from_cuda(launch_rope(as_stream(stream), d, x, x_nb1 / 4, out, out_nb1 / 4, pos, n_rows, row_len));
+}
+
+cvattn_status cvattn_kv_append_rope(cvattn_context* ctx, void* stream, const cvattn_tensor* cache, const float* src,
+                                    int64_t src_nb1, int64_t src_nb2, const int32_t* pos, int64_t pos_nb1,
+                                    int32_t n_new, int32_t batch, const cvattn_rope_params* rope) {
+    RopeDev d;
+    if (!rope_dev(rope, d) || !tensor_ok(cache) || (cache->n_heads * cache->head_dim) % rope->unit_len)
+        return CVATTN_ERR_INVALID_ARGUMENT;
+    if (!ctx || n_new < 0 || batch < 0 || batch > cache->ne2) return CVATTN_ERR_INVALID_ARGUMENT;
+    if (n_new == 0 || batch == 0) return CVATTN_OK;
+    if (!src || !pos || (src_nb1 & 3) || (src_nb2 & 3) || (pos_nb1 & 3) || pos_nb1 < 0)
+        return CVATTN_ERR_INVALID_ARGUMENT;
+    if (reinterpret_cast<uintptr_t>(src) & 3) return CVATTN_ERR_INVALID_ARGUMENT;
+    return from_cuda(launch_kv_append(as_stream(stream), *cache, src, src_nb1, src_nb2, pos, pos_nb1 / 4, n_new, batch,
+                                      ctx->status, &d));
+}
+
 cvattn_status cvattn_kv_dequantize(cvattn_context* ctx, void* stream, const cvattn_tensor* cache, int32_t n_rows,
                                    float* dst) {
     if (!ctx || !tensor_ok(cache) || n_rows < 0 || n_rows > cache->ne1 || (n_rows && !dst))
@@ -293,7 +345,8 @@ cvattn_status cvattn_workspace_init(void* stream, void* workspace, size_t bytes)
     return from_cuda(cudaMemsetAsync(workspace, 0, bytes, as_stream(stream)));
 }
 
-cvattn_status cvattn_decode(cvattn_context* ctx, void* stream, const cvattn_decode_params* p) {
+static cvattn_status decode_impl(cvattn_context* ctx, void* stream, const cvattn_decode_params* p,
+                                 const cvattn_rope_params* rope) {
     if (!ctx || !p || !p->q || !p->out || !p->kv_len) return CVATTN_ERR_INVALID_ARGUMENT;
     if (p->n_seq < 0 || p->max_kv_len < 0 || p->n_q_heads <= 0) return CVATTN_ERR_INVALID_ARGUMENT;
     if (p->n_seq == 0) return CVATTN_OK;
@@ -322,6 +375,12 @@ cvattn_status cvattn_decode(cvattn_context* ctx, void* stream, const cvattn_deco
     const size_t need = decode_workspace_bytes(k.type, v.type, p->n_seq, p->max_kv_len, p->n_q_heads, k.n_heads,
                                                k.head_dim);
     if (!p->workspace || p->workspace_size < need) return CVATTN_ERR_INVALID_ARGUMENT;
+    RopeDev rd;
+    if (rope) {
+        if (!rope_dev(rope, rd)) return CVATTN_ERR_INVALID_ARGUMENT;
+        if (rope->unit_len != k.head_dim || rope->n_dims != k.head_dim || !decode_rope_supported(*p))
+            return CVATTN_ERR_UNSUPPORTED;
+    }
     if (p->max_kv_len == 0) {
         // nothing visible anywhere: ggml's S == 0 convention gives zeros
         for (int32_t s = 0; s < p->n_seq; ++s) {
@@ -331,7 +390,17 @@ cvattn_status cvattn_decode(cvattn_context* ctx, void* stream, const cvattn_deco
         }
         return CVATTN_OK;
     }
-    return from_cuda(launch_decode(as_stream(stream), *p, ctx->status));
+    return from_cuda(launch_decode(as_stream(stream), *p, ctx->status, rope ? &rd : nullptr));
+}
+
+cvattn_status cvattn_decode(cvattn_context* ctx, void* stream, const cvattn_decode_params* p) {
+    return decode_impl(ctx, stream, p, nullptr);
+}
+
+cvattn_status cvattn_decode_rope(cvattn_context* ctx, void* stream, const cvattn_decode_params* p,
+                                 const cvattn_rope_params* rope) {
+    if (!rope) return CVATTN_ERR_INVALID_ARGUMENT;
+    return decode_impl(ctx, stream, p, rope);
 }
 
 cvattn_status cvattn_combine(void* stream, const float* partial_o, const float* partial_ml, int32_t n_parts,

@@ -5,6 +5,7 @@
 #include "decode_stream.cuh"
 #include "decode_tc.cuh"
 #include "internal.h"
+#include "rope.cuh"
 
 namespace cvattn {
 
@@ -45,7 +46,16 @@ size_t decode_workspace_bytes(int k_type, int v_type, int n_seq, int max_kv_len,
            align256((size_t)n_seq * chunks * n_q_heads * kD * 4);
 }
 
-cudaError_t launch_decode(cudaStream_t stream, const cvattn_decode_params& p, int* status) {
+bool decode_rope_supported(const cvattn_decode_params& p) {
+    const int Hkv = p.k.n_heads;
+    const int G = Hkv > 0 ? p.n_q_heads / Hkv : 0;
+    return !(p.flags & (CVATTN_DECODE_CUDA_CORES | CVATTN_DECODE_NOT_PERSISTENT | CVATTN_DECODE_WIDE_CHUNKS)) &&
+           Hkv == 2 && p.k.head_dim == kD && G >= 1 && G <= dtc::kHP && dstream::supported_type(p.k.type) &&
+           dstream::supported_type(p.v.type) && p.n_seq <= dstream::kMaxSeq &&
+           dstream::smem_bytes(p.k.type, p.v.type) <= 227 * 1024;
+}
+
+cudaError_t launch_decode(cudaStream_t stream, const cvattn_decode_params& p, int* status, const RopeDev* rope) {
     const int Hkv = p.k.n_heads;
     const int C = decode_chunk_positions(p.k.type, p.v.type, Hkv, p.k.head_dim);
     const int chunks = (p.max_kv_len + C - 1) / C;
@@ -73,6 +83,13 @@ cudaError_t launch_decode(cudaStream_t stream, const cvattn_decode_params& p, in
     a.flags = p.flags;
     a.max_kv_len = p.max_kv_len;
     a.scale_log2 = p.scale * 1.4426950408889634f;
+    if (rope) {
+        a.rope_mode = rope->mode;
+        a.rope_n_dims = rope->n_dims;
+        a.rope_theta_scale = rope->theta_scale;
+        a.rope_freq_scale = rope->freq_scale;
+        a.rope_attn_factor = rope->attn_factor;
+    }
     uint8_t* ws = static_cast<uint8_t*>(p.workspace);
     const size_t cnt_bytes = align256((size_t)p.n_seq * 4);
     const size_t ml_bytes = align256((size_t)p.n_seq * chunks * p.n_q_heads * 2 * 4);
@@ -118,6 +135,7 @@ cudaError_t launch_decode(cudaStream_t stream, const cvattn_decode_params& p, in
             default: break;
             }
         }
+        if (a.rope_n_dims > 0) return cudaErrorNotSupported;  // only the streaming kernel applies a RoPE
         if (persistent && dpipe::supported_type(p.k.type) &&
             dpipe::supported_type(p.v.type) && p.n_seq <= dpipe::kMaxSeq &&
             dpipe::smem_bytes(p.k.type, p.v.type) <= 227 * 1024) {

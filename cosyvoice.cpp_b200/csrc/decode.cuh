@@ -59,6 +59,10 @@ struct Args {
     uint32_t* ws_cnt;
     int ws_chunks;  // chunk stride of the workspace arrays
     int* status;
+    // RoPE of Q and the appended K row at position kv_len - 1 (streaming kernel;
+    // rope_n_dims = 0: none)
+    int rope_mode, rope_n_dims;
+    float rope_theta_scale, rope_freq_scale, rope_attn_factor;
 };
 
 // Shared-memory carve-up, identical on host and device.

@@ -45,6 +45,7 @@
 #pragma once
 
 #include "decode_pipe.cuh"
+#include "rope.cuh"
 
 namespace cvattn {
 namespace dstream {
@@ -531,14 +532,50 @@ __global__ void __launch_bounds__(640, 1) decode_stream_kernel(const Args a) {
         // sums over a K block: built once per sequence
         uint4 qw[2];
         float qe[2], qs[2];
+        const RopeDev rope{a.rope_mode, a.rope_n_dims, kD, a.rope_theta_scale, a.rope_freq_scale, a.rope_attn_factor};
+        int seq = 0, chunk = 0;  // cursor of the group's current item
         auto build_q = [&]() {
 #pragma unroll
             for (int qi = 0; qi < 2; ++qi) {
                 const int item = ctid + qi * 128;
-                const int row = (item >> 3) & 15;
+                const int row = (item >> 3) & 15, cc = item & 7;
                 const bool lo_row = row >= 8;
                 const float4 u = qv[qi][0], v = qv[qi][1];
-                const float x[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
+                float x[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
+                if (rope.n_dims > 0) {  // Q turns by the new token's position (n_dims = head_dim)
+                    const int p = slen[seq] - 1;
+                    float y[8];
+                    int k0;
+                    bool first = true;
+                    if (rope.mode & 2) {  // NEOX: partner dims d +- 32 live in lane cc ^ 4
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) y[e] = __shfl_xor_sync(0xffffffffu, x[e], 4);
+                        first = cc < 4;
+                        k0 = 8 * (cc & 3);
+                    } else {  // NORMAL: partner dim d ^ 1 is in this thread
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) y[e] = x[e ^ 1];
+                        k0 = 4 * cc;
+                    }
+                    float theta = rope_theta(rope, p, k0);
+                    float2 cs = rope_cs(rope, theta);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        if (rope.mode & 2) {
+                            if (e > 0) {
+                                theta = rope_next(rope, theta);
+                                cs = rope_cs(rope, theta);
+                            }
+                            x[e] = rope_rotate(x[e], y[e], cs, first);
+                        } else {
+                            if (e > 0 && (e & 1) == 0) {
+                                theta = rope_next(rope, theta);
+                                cs = rope_cs(rope, theta);
+                            }
+                            x[e] = rope_rotate(x[e], y[e], cs, (e & 1) == 0);
+                        }
+                    }
+                }
                 float am = 0.0f, part = 0.0f;
 #pragma unroll
                 for (int e = 0; e < 8; ++e) { am = fmaxf(am, fabsf(x[e])); part += x[e]; }
@@ -560,7 +597,6 @@ __global__ void __launch_bounds__(640, 1) decode_stream_kernel(const Args a) {
                 qs[qi] = part * a.scale_log2;
             }
         };
-        int seq = 0, chunk = 0;
         bool q_dirty = true;  // qv holds a sequence's Q that qw / qe / qs do not reflect yet
         if (c < n_local) {
             item_of(pref, n_seq, item_at(c), seq, chunk);
@@ -598,7 +634,15 @@ __global__ void __launch_bounds__(640, 1) decode_stream_kernel(const Args a) {
                 for (int gi = cw; gi < 8; gi += 4) {
                     const bool isv = gi >= 4;
                     const int g2 = gi & 3;
-                    const float xv = (isv ? a.v_new : a.k_new)[(int64_t)seq * 2 * kD + g2 * 32 + lane];
+                    float xv = (isv ? a.v_new : a.k_new)[(int64_t)seq * 2 * kD + g2 * 32 + lane];
+                    if (!isv && rope.n_dims > 0) {  // the new K row turns by position len - 1
+                        const float* krow = a.k_new + (int64_t)seq * 2 * kD + (g2 >> 1) * kD;  // its head
+                        const int d = (g2 & 1) * 32 + lane;
+                        int k;
+                        bool first;
+                        const int pd = rope_pair(rope, d, k, first);
+                        xv = rope_rotate(xv, krow[pd], rope_cs(rope, rope_theta(rope, len - 1, k)), first);
+                    }
                     if (!isv) {
                         quantize_block_warp<KT>(xv, Kraw + rr * rowK + g2 * GBK, lane);
                         quantize_block_warp<KT>(xv, const_cast<uint8_t*>(kb) + (int64_t)(len - 1) * rowK + g2 * GBK, lane);

@@ -6,8 +6,13 @@
 // One warp handles one 32-element group of one row; blocks are bit-identical
 // to ggml's reference quantizers (see quantize_block_warp in common.cuh).
 // HBM-bound: reads 128 B of f32 per group, writes 18-128 B.
+//
+// With a RoPE the K rows are rotated on the way in, as ggml_rope_ext does
+// before update_cache (src/cosyvoice-llm.cpp:57,180; src/cosyvoice-graph.cpp:355);
+// the standalone rope kernel covers Q and other callers.
 #include "common.cuh"
 #include "internal.h"
+#include "rope.cuh"
 
 namespace cvattn {
 
@@ -15,7 +20,7 @@ template <int T>
 __global__ void __launch_bounds__(256) kv_append_kernel(
     uint8_t* __restrict__ cache, int64_t nb1, int64_t nb2, int64_t capacity, int groups_per_row,
     const float* __restrict__ src, int64_t src_nb1, int64_t src_nb2,
-    const int32_t* __restrict__ pos, int64_t pos_stride, int n_new, int batch, int* status) {
+    const int32_t* __restrict__ pos, int64_t pos_stride, int n_new, int batch, int* status, RopeDev rope) {
     const int lane = threadIdx.x & 31;
     const int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int64_t total = (int64_t)n_new * batch * groups_per_row;
@@ -29,10 +34,42 @@ __global__ void __launch_bounds__(256) kv_append_kernel(
         if (lane == 0) record_status(status, kStatusBadPosition);
         return;
     }
-    const float x = *reinterpret_cast<const float*>(
-        reinterpret_cast<const uint8_t*>(src) + t * src_nb1 + b * src_nb2 + ((int64_t)g * 32 + lane) * 4);
+    const float* row = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(src) + t * src_nb1 + b * src_nb2);
+    const int e = g * 32 + lane;
+    float x = row[e];
+    if (rope.n_dims > 0) {
+        int k;
+        bool first;
+        const int pe = rope_pair(rope, e, k, first);
+        if (pe >= 0) x = rope_rotate(x, row[pe], rope_cs(rope, rope_theta(rope, p, k)), first);
+    }
     uint8_t* dst = cache + b * nb2 + (int64_t)p * nb1 + (int64_t)g * group_bytes(T);
     quantize_block_warp<T>(x, dst, lane);
+}
+
+// Standalone RoPE: rows of row_len floats (row r at x + r * x_nb1f, out + r * out_nb1f;
+// x may equal out).  One thread per pair (or per unrotated element), so a pair
+// is read before either of its elements is written.
+__global__ void __launch_bounds__(256) rope_kernel(const float* x, int64_t x_nb1f, float* out, int64_t out_nb1f,
+                                                   const int32_t* __restrict__ pos, int n_rows, int row_len,
+                                                   RopeDev rope) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (int64_t)n_rows * row_len) return;
+    const int r = (int)(idx / row_len), e = (int)(idx % row_len);
+    const float* xr = x + r * x_nb1f;
+    float* orow = out + r * out_nb1f;
+    int k;
+    bool first;
+    const int pe = rope_pair(rope, e, k, first);
+    if (pe < 0) {
+        orow[e] = xr[e];
+        return;
+    }
+    if (!first) return;  // the pair's first element writes both
+    const float a = xr[e], bb = xr[pe];
+    const float2 cs = rope_cs(rope, rope_theta(rope, pos[r], k));
+    orow[e] = rope_rotate(a, bb, cs, true);
+    orow[pe] = rope_rotate(bb, a, cs, false);
 }
 
 template <int T>
@@ -53,7 +90,8 @@ __global__ void __launch_bounds__(256) kv_dequant_kernel(
 
 cudaError_t launch_kv_append(cudaStream_t stream, const cvattn_tensor& c, const float* src, int64_t src_nb1,
                              int64_t src_nb2, const int32_t* pos, int64_t pos_stride, int n_new, int batch,
-                             int* status) {
+                             int* status, const RopeDev* rope) {
+    const RopeDev rp = rope ? *rope : RopeDev{0, 0, 1, 1.0f, 1.0f, 1.0f};
     const int row_elems = c.n_heads * c.head_dim;
     const int groups = row_elems / 32;
     const int64_t warps = (int64_t)n_new * batch * groups;
@@ -63,7 +101,7 @@ cudaError_t launch_kv_append(cudaStream_t stream, const cvattn_tensor& c, const 
 #define CVATTN_APPEND_CASE(T)                                                                              \
     case T:                                                                                                \
         kv_append_kernel<T><<<grid, 256, 0, stream>>>(base, c.nb1, c.nb2, c.ne1, groups, src, src_nb1,     \
-                                                      src_nb2, pos, pos_stride, n_new, batch, status);     \
+                                                      src_nb2, pos, pos_stride, n_new, batch, status, rp); \
         break;
     switch (c.type) {
         CVATTN_APPEND_CASE(kF32)
@@ -76,6 +114,14 @@ cudaError_t launch_kv_append(cudaStream_t stream, const cvattn_tensor& c, const 
     default: return cudaErrorInvalidValue;
     }
 #undef CVATTN_APPEND_CASE
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rope(cudaStream_t stream, const RopeDev& rope, const float* x, int64_t x_nb1f, float* out,
+                        int64_t out_nb1f, const int32_t* pos, int n_rows, int row_len) {
+    const int64_t n = (int64_t)n_rows * row_len;
+    if (n == 0) return cudaSuccess;
+    rope_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(x, x_nb1f, out, out_nb1f, pos, n_rows, row_len, rope);
     return cudaGetLastError();
 }
 

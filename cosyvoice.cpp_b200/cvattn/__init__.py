@@ -14,7 +14,7 @@ import math
 from typing import Sequence
 
 from . import _lib
-from ._lib import DecodeParams, DitStep, FlashParams, KVCacheParams, Tensor, load
+from ._lib import DecodeParams, DitStep, FlashParams, KVCacheParams, RopeParams, Tensor, load
 
 # ggml type ids
 F32, F16, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0 = 0, 1, 2, 3, 6, 7, 8
@@ -32,6 +32,7 @@ DECODE_NOT_PERSISTENT = 4
 DECODE_INPUTS_READY = 8
 DECODE_WIDE_CHUNKS = 16
 FLASH_ONE_TILE = 1
+ROPE_NORMAL, ROPE_NEOX = 0, 2
 
 OK = 0
 STATUS_NAMES = {0: "OK", 1: "INVALID_ARGUMENT", 2: "UNSUPPORTED", 3: "LENGTH", 4: "ALLOC", 5: "CUDA",
@@ -150,15 +151,42 @@ def alloc_kv(type_: int, n_heads: int, head_dim: int, ne1: int, ne2: int = 1, de
     return buf, kv_tensor(buf, type_, n_heads, head_dim, ne1, ne2)
 
 
-def kv_append(ctx: Context, cache: Tensor, src, pos, stream=None) -> None:
+def rope_params(mode: int, n_dims: int, unit_len: int, freq_base: float, freq_scale: float = 1.0,
+                attn_factor: float = 1.0) -> RopeParams:
+    """A ggml_rope_ext description (ext_factor 0): NEOX per head for the LLM
+    (src/cosyvoice-llm.cpp:56-57), NORMAL on the row prefix for the DiT
+    (src/cosyvoice-graph.cpp:354-355)."""
+    return RopeParams(mode, n_dims, unit_len, freq_base, freq_scale, attn_factor)
+
+
+def rope(x, pos, rp: RopeParams, out=None, stream=None):
+    """RoPE of f32 rows x [..., row_len] (contiguous) at positions pos (int32, one per row)."""
+    torch = _torch()
+    assert x.dtype == torch.float32 and x.is_contiguous()
+    row_len = x.shape[-1]
+    n_rows = x.numel() // row_len
+    if out is None:
+        out = torch.empty_like(x)
+    check(lib.cvattn_rope(_stream(stream), ctypes.byref(rp), x.data_ptr(), row_len * 4, out.data_ptr(), row_len * 4,
+                          pos.data_ptr(), n_rows, row_len), "rope")
+    return out
+
+
+def kv_append(ctx: Context, cache: Tensor, src, pos, stream=None, rope: RopeParams | None = None) -> None:
     """ggml_set_rows into the cache: src f32 [batch, n_new, row] contiguous,
-    pos int32 [n_new] (shared) or [batch, n_new] on the device."""
+    pos int32 [n_new] (shared) or [batch, n_new] on the device.  With rope the
+    rows turn by their positions first (the key RoPE fused with the append)."""
     torch = _torch()
     assert src.dtype == torch.float32 and src.is_contiguous() and src.dim() == 3
     batch, n_new, row = src.shape
     pos_nb1 = 0 if pos.dim() == 1 else pos.stride(0) * 4
-    check(lib.cvattn_kv_append(ctx.handle, _stream(stream), ctypes.byref(cache), src.data_ptr(), row * 4,
-                               n_new * row * 4, pos.data_ptr(), pos_nb1, n_new, batch), "kv_append")
+    if rope is None:
+        check(lib.cvattn_kv_append(ctx.handle, _stream(stream), ctypes.byref(cache), src.data_ptr(), row * 4,
+                                   n_new * row * 4, pos.data_ptr(), pos_nb1, n_new, batch), "kv_append")
+    else:
+        check(lib.cvattn_kv_append_rope(ctx.handle, _stream(stream), ctypes.byref(cache), src.data_ptr(), row * 4,
+                                        n_new * row * 4, pos.data_ptr(), pos_nb1, n_new, batch, ctypes.byref(rope)),
+              "kv_append_rope")
 
 
 def kv_dequantize(ctx: Context, cache: Tensor, n_rows: int, stream=None):
@@ -188,8 +216,9 @@ class Decoder:
                  q, out, kv_len, k_new=None, v_new=None, k_seq_ptrs=None, v_seq_ptrs=None,
                  scale: float | None = None, emit_partial: bool = False, partial_ml=None, workspace=None,
                  cuda_cores: bool = False, not_persistent: bool = False, inputs_ready: bool = False,
-                 wide_chunks: bool = False):
+                 wide_chunks: bool = False, rope: RopeParams | None = None):
         self.ctx = ctx
+        self.rope = rope
         p = DecodeParams()
         p.q, p.q_seq_stride = q.data_ptr(), q.stride(0)
         p.out, p.out_seq_stride = out.data_ptr(), out.stride(0)
@@ -212,7 +241,11 @@ class Decoder:
         self._keep = (q, out, kv_len, k_new, v_new, k_seq_ptrs, v_seq_ptrs, partial_ml)
 
     def __call__(self, stream=None) -> None:
-        check(lib.cvattn_decode(self.ctx.handle, _stream(stream), ctypes.byref(self.params)), "decode")
+        if self.rope is None:
+            check(lib.cvattn_decode(self.ctx.handle, _stream(stream), ctypes.byref(self.params)), "decode")
+        else:
+            check(lib.cvattn_decode_rope(self.ctx.handle, _stream(stream), ctypes.byref(self.params),
+                                         ctypes.byref(self.rope)), "decode_rope")
 
 
 def decode(ctx: Context, q, k: Tensor, v: Tensor, kv_len, max_kv_len: int, out=None, **kw):

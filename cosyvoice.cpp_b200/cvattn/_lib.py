@@ -64,7 +64,14 @@ class DitStep(ctypes.Structure):
     ]
 
 
-STRUCTS = {0: Tensor, 1: DecodeParams, 2: FlashParams, 3: KVCacheParams, 4: DitStep}
+class RopeParams(ctypes.Structure):
+    _fields_ = [
+        ("mode", c_int32), ("n_dims", c_int32), ("unit_len", c_int32),
+        ("freq_base", ctypes.c_float), ("freq_scale", ctypes.c_float), ("attn_factor", ctypes.c_float),
+    ]
+
+
+STRUCTS = {0: Tensor, 1: DecodeParams, 2: FlashParams, 3: KVCacheParams, 4: DitStep, 5: RopeParams}
 
 # (name, restype, argtypes) for every symbol include/cvattn.h declares.
 P = ctypes.POINTER
@@ -86,10 +93,14 @@ SIGNATURES = [
     ("cvattn_kv_append", c_int32,
      [c_void_p, c_void_p, P(Tensor), c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int32, c_int32]),
     ("cvattn_kv_dequantize", c_int32, [c_void_p, c_void_p, P(Tensor), c_int32, c_void_p]),
+    ("cvattn_rope", c_int32, [c_void_p, P(RopeParams), c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int32, c_int32]),
+    ("cvattn_kv_append_rope", c_int32,
+     [c_void_p, c_void_p, P(Tensor), c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int32, c_int32, P(RopeParams)]),
     ("cvattn_decode_workspace_size", c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32]),
     ("cvattn_workspace_init", c_int32, [c_void_p, c_void_p, c_size_t]),
     ("cvattn_decode", c_int32, [c_void_p, c_void_p, P(DecodeParams)]),
     ("cvattn_decode_noalloc", c_int32, [c_void_p, c_void_p, P(DecodeParams)]),
+    ("cvattn_decode_rope", c_int32, [c_void_p, c_void_p, P(DecodeParams), P(RopeParams)]),
     ("cvattn_combine", c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p]),
     ("cvattn_flash", c_int32, [c_void_p, c_void_p, P(FlashParams)]),
     ("cvattn_kv_copy_to_host", c_int32, [c_void_p, P(Tensor), c_int32, c_void_p]),

@@ -54,7 +54,7 @@ int32_t cvattn_status_to_ggml(cvattn_status s);
 
 /* ABI version and struct sizes, so bindings can verify their mirrors.
  * which: 0 cvattn_tensor, 1 cvattn_decode_params, 2 cvattn_flash_params,
- *        3 cvattn_kv_cache_params, 4 cvattn_dit_step. */
+ *        3 cvattn_kv_cache_params, 4 cvattn_dit_step, 5 cvattn_rope_params. */
 int32_t cvattn_abi_version(void);
 size_t cvattn_abi_sizeof(int32_t which);
 
@@ -140,6 +140,48 @@ cvattn_status cvattn_kv_append(cvattn_context* ctx, void* stream, const cvattn_t
                                const int32_t* pos, int64_t pos_nb1,
                                int32_t n_new, int32_t batch);
 
+/* ------------------------------------------------------------------- RoPE */
+
+/* Rotary position embedding as ggml_rope_ext applies it in the reference, with
+ * ext_factor 0 and no frequency factors (the only form it uses):
+ *   LLM  src/cosyvoice-llm.cpp:56-57,180  NEOX, n_dims = unit_len = head_dim,
+ *        freq_base = rope_theta, freq_scale 1, attn_factor 1;
+ *   DiT  src/cosyvoice-graph.cpp:354-355  NORMAL, n_dims = head_dim on the
+ *        whole 1024-wide row (unit_len = row length), freq_base 10000.
+ * Angles follow ggml's CPU backend: theta_scale = powf(freq_base, -2/n_dims)
+ * (formed on the host), pair k at position p turns by p * theta_scale^k built
+ * by k sequential float products, times freq_scale. */
+enum {
+    CVATTN_ROPE_NORMAL = 0,  /* pairs (2k, 2k + 1)          (GGML_ROPE_TYPE_NORMAL) */
+    CVATTN_ROPE_NEOX = 2     /* pairs (k, k + n_dims / 2)   (GGML_ROPE_TYPE_NEOX)   */
+};
+
+typedef struct cvattn_rope_params {
+    int32_t mode;         /* CVATTN_ROPE_NORMAL or CVATTN_ROPE_NEOX */
+    int32_t n_dims;       /* rotated prefix of each unit: even, 2..unit_len */
+    int32_t unit_len;     /* elements per rotation unit: head_dim, or the whole row */
+    float   freq_base;    /* rope_theta */
+    float   freq_scale;
+    float   attn_factor;  /* scales cos and sin */
+} cvattn_rope_params;
+
+/* out = RoPE(x) for n_rows rows of row_len f32 (row r at x + r*x_nb1 and
+ * out + r*out_nb1 bytes; out may equal x), row r at position pos[r] (device
+ * int32).  row_len must be a multiple of unit_len. */
+cvattn_status cvattn_rope(void* stream, const cvattn_rope_params* rope,
+                          const float* x, int64_t x_nb1, float* out, int64_t out_nb1,
+                          const int32_t* pos, int32_t n_rows, int32_t row_len);
+
+/* cvattn_kv_append with the K rows rotated on the way in: the ggml_rope_ext of
+ * the keys fused with update_cache (src/cosyvoice-llm.cpp:57-59,180-182;
+ * src/cosyvoice-graph.cpp:355,365).  Row (t, b) turns by its cache position
+ * pos[t + b*pos_nb1/4].  The bytes equal cvattn_rope followed by
+ * cvattn_kv_append. */
+cvattn_status cvattn_kv_append_rope(cvattn_context* ctx, void* stream, const cvattn_tensor* cache,
+                                    const float* src, int64_t src_nb1, int64_t src_nb2,
+                                    const int32_t* pos, int64_t pos_nb1,
+                                    int32_t n_new, int32_t batch, const cvattn_rope_params* rope);
+
 /* Dequantize rows [0, n_rows) of every batch entry to f32
  * (dst row (t, b) at dst + (b*n_rows + t)*n_heads*head_dim).  Used for the
  * offload of a slot to f32 and by tests. */
@@ -222,6 +264,16 @@ cvattn_status cvattn_decode(cvattn_context* ctx, void* stream, const cvattn_deco
  *     remain in the array. */
 #define CVATTN_DECODE_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
 cvattn_status cvattn_decode_noalloc(cvattn_context* ctx, void* stream, const cvattn_decode_params* p);
+
+/* cvattn_decode with the RoPE of the decode step fused in: Q and the appended
+ * K row of sequence s turn by position kv_len[s] - 1 (the ggml_rope_ext calls
+ * of src/cosyvoice-llm.cpp:56-57 before update_cache and attention_forward).
+ * Runs on the default streaming kernel, so it needs block-quantized K and V,
+ * 2 KV heads, head_dim 64, at most 512 sequences, no flag that selects
+ * another kernel, and a per-head rope (unit_len = n_dims = head_dim);
+ * otherwise CVATTN_ERR_UNSUPPORTED (use cvattn_rope, then cvattn_decode). */
+cvattn_status cvattn_decode_rope(cvattn_context* ctx, void* stream, const cvattn_decode_params* p,
+                                 const cvattn_rope_params* rope);
 
 /* Log-sum-exp combine of split partials (cross-GPU split-KV):
  *   partial_o  f32 [n_parts][n_rows][head_dim] unnormalized

@@ -24,6 +24,11 @@
  *     not available to run); the fp64 restatement is the numeric oracle.
  *   - build_causal_mask (src/cosyvoice-llm.cpp:20-29) and the DiT chunk mask
  *     fill (src/cosyvoice-token2wav.cpp:285-298).
+ *   - ggml_rope_ext as the reference calls it before the KV append and the
+ *     attention (src/cosyvoice-llm.cpp:56-57,180 NEOX per head;
+ *     src/cosyvoice-graph.cpp:354-355 NORMAL on the first head_dim elements
+ *     of the whole row), restated from ggml's CPU backend (parity unpinned:
+ *     ggml is not available to run).
  *   - A ggml-CPU-style single-pass fp32 flash attention (online max / sum per
  *     query row, K/V rows dequantized on the fly) used as the timed CPU
  *     baseline because ggml's own CPU kernel cannot be built here.
@@ -484,6 +489,49 @@ void oracle_flash_cpu(const float* q, int32_t n_seq, int32_t n_q, int32_t Hq, in
         free(vbuf);
         free(acc);
     }
+}
+
+/* ---------------------------------------------------------------- RoPE -- */
+
+/* Rotary position embedding, ggml_rope_ext with ext_factor 0 and no frequency
+ * factors (the only form the reference uses: freq_scale 1, attn_factor 1).
+ * ggml's CPU backend forms theta_scale = powf(freq_base, -2/n_dims) and, per
+ * position p, the angle of pair k as p * theta_scale^k by k sequential float
+ * products, then freq_scale * angle; cos / sin are cosf / sinf times
+ * attn_factor.  Rows are cut into units of unit_len elements (a head for the
+ * LLM, the whole row for the DiT); in each unit the first n_dims elements
+ * rotate in pairs -- NEOX: element i with i + n_dims/2; NORMAL: 2k with
+ * 2k + 1 -- as out_a = a cos - b sin, out_b = a sin + b cos (two rounded
+ * products and one rounded sum each), and the rest is copied.
+ * x and out: n_rows rows of row_len floats (row r at x + r * row_len). */
+void oracle_rope(const float* x, float* out, const int32_t* pos, int32_t n_rows, int32_t row_len, int32_t unit_len,
+                 int32_t n_dims, int32_t mode, float freq_base, float freq_scale, float attn_factor)
+{
+    const int neox = (mode & 2) != 0;
+    const int half = n_dims / 2;
+    const float theta_scale = powf(freq_base, -2.0f / (float)n_dims);
+    float* cs = (float*)malloc(sizeof(float) * 2 * (half > 0 ? half : 1));
+    for (int32_t r = 0; r < n_rows; ++r) {
+        float theta = (float)pos[r];
+        for (int k = 0; k < half; ++k) {
+            const float th = freq_scale * theta;
+            cs[2 * k] = cosf(th) * attn_factor;
+            cs[2 * k + 1] = sinf(th) * attn_factor;
+            theta *= theta_scale;
+        }
+        const float* xr = x + (int64_t)r * row_len;
+        float* orow = out + (int64_t)r * row_len;
+        for (int32_t u = 0; u + unit_len <= row_len; u += unit_len) {
+            for (int k = 0; k < half; ++k) {
+                const int i0 = neox ? k : 2 * k, i1 = neox ? k + half : 2 * k + 1;
+                const float a = xr[u + i0], b = xr[u + i1], c = cs[2 * k], sn = cs[2 * k + 1];
+                orow[u + i0] = a * c - b * sn;
+                orow[u + i1] = a * sn + b * c;
+            }
+            for (int i = n_dims; i < unit_len; ++i) orow[u + i] = xr[u + i];
+        }
+    }
+    free(cs);
 }
 
 int oracle_max_threads(void)

@@ -70,6 +70,8 @@ def lib():
             c.c_int32, c.c_void_p, c.c_int64,
             c.c_void_p, c.c_int32, c.c_float, c.c_void_p, c.c_int32,
         ]
+        L.oracle_rope.argtypes = [c.c_void_p, c.c_void_p, c.c_void_p, c.c_int32, c.c_int32, c.c_int32,
+                                  c.c_int32, c.c_int32, c.c_float, c.c_float, c.c_float]
         L.oracle_max_threads.restype = c.c_int
         _lib = L
     return _lib
@@ -103,6 +105,24 @@ def dequantize(t: int, q: np.ndarray, n: int) -> np.ndarray:
     out = np.empty(q.shape[:-1] + (n,), dtype=np.float32)
     if lib().oracle_dequantize_rows(t, _ptr(q), rows, n, _ptr(out)):
         raise ValueError("dequantize failed")
+    return out
+
+
+ROPE_NORMAL, ROPE_NEOX = 0, 2
+
+
+def rope(x: np.ndarray, pos: np.ndarray, unit_len: int, n_dims: int, mode: int, freq_base: float,
+         freq_scale: float = 1.0, attn_factor: float = 1.0) -> np.ndarray:
+    """ggml_rope_ext (ext_factor 0) on rows x[..., row_len] at positions pos[rows]
+    (src/cosyvoice-llm.cpp:56-57,180; src/cosyvoice-graph.cpp:354-355)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    row_len = x.shape[-1]
+    rows = x.size // row_len
+    p = np.ascontiguousarray(pos, dtype=np.int32).reshape(-1)
+    assert p.size == rows and row_len % unit_len == 0 and n_dims % 2 == 0 and n_dims <= unit_len
+    out = np.empty_like(x)
+    lib().oracle_rope(_ptr(x), _ptr(out), _ptr(p), rows, row_len, unit_len, n_dims, mode,
+                      float(freq_base), float(freq_scale), float(attn_factor))
     return out
 
 
