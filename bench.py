@@ -260,6 +260,8 @@ def run_ours(args, rank: int, world: int, torch, dist) -> dict | None:
     if rank == 0 and not args.skip_secondary:
         secondary = run_flash_secondary(torch, cv, ctx, args)
         secondary.update(run_decode_cfg4(torch, cv, ctx))
+        secondary.update(run_decode_rope(torch, cv, ctx, caches, q, k_new, v_new, out, kv_len, bytes_per_layer,
+                                         launch_us))
     del graph
     if rank != 0:
         return None
@@ -300,6 +302,46 @@ def run_ours(args, rank: int, world: int, torch, dist) -> dict | None:
         "clocks": clocks.summary(),
         **secondary,
     }
+
+
+def run_decode_rope(torch, cv, ctx, caches, q, k_new, v_new, out, kv_len, bytes_per_layer: int, launch_us: float,
+                    reps: int = 20) -> dict:
+    """The headline step with the decode RoPE fused in (Q and the appended K row
+    turn by kv_len - 1; NEOX, rope_theta 1e6, src/cosyvoice-llm.cpp:56-57): the
+    same 24-launch graph through cvattn_decode_rope."""
+    rp = cv.rope_params(cv.ROPE_NEOX, D, D, 1_000_000.0)
+    decs = [cv.Decoder(ctx, caches[l][1], caches[l][3], N_SEQ, HQ, CAP, q[l], out[l], kv_len,
+                       k_new=k_new[l], v_new=v_new[l], inputs_ready=True, rope=rp) for l in range(LAYERS)]
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            for d in decs:
+                d(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        graph.capture_begin()
+        for d in decs:
+            d(stream)
+        graph.capture_end()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / reps / LAYERS
+    del graph
+    st, detail = ctx.sync_status()
+    if st != 0:
+        raise RuntimeError(f"device status {st} ({detail}) after the RoPE decode")
+    return {"decode_rope": {"what": "headline step with the Q / K RoPE fused into decode (NEOX, theta 1e6)",
+                            "us_per_launch": round(us, 3), "gbs": round(bytes_per_layer / (us * 1e-6) / 1e9, 1),
+                            "without_rope_us_per_launch": round(launch_us, 3)}}
 
 
 def build_cfg4(torch, cv, ctx, kt: int, vt: int, gen):
