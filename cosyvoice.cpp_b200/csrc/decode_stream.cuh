@@ -535,6 +535,10 @@ __global__ void __launch_bounds__(640, 1) decode_stream_kernel(const Args a) {
         const RopeDev rope{a.rope_mode, a.rope_n_dims, kD, a.rope_theta_scale, a.rope_freq_scale, a.rope_attn_factor};
         int seq = 0, chunk = 0;  // cursor of the group's current item
         auto build_q = [&]() {
+            // (cos, sin) of pair k = lane at the new token's position: one sincosf per lane,
+            // handed to the elements that need it by shuffles
+            float2 qcs = make_float2(1.0f, 0.0f);
+            if (rope.n_dims > 0) qcs = rope_cs(rope, rope_theta(rope, slen[seq] - 1, lane));
 #pragma unroll
             for (int qi = 0; qi < 2; ++qi) {
                 const int item = ctid + qi * 128;
@@ -543,37 +547,22 @@ __global__ void __launch_bounds__(640, 1) decode_stream_kernel(const Args a) {
                 const float4 u = qv[qi][0], v = qv[qi][1];
                 float x[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
                 if (rope.n_dims > 0) {  // Q turns by the new token's position (n_dims = head_dim)
-                    const int p = slen[seq] - 1;
                     float y[8];
-                    int k0;
                     bool first = true;
                     if (rope.mode & 2) {  // NEOX: partner dims d +- 32 live in lane cc ^ 4
 #pragma unroll
                         for (int e = 0; e < 8; ++e) y[e] = __shfl_xor_sync(0xffffffffu, x[e], 4);
                         first = cc < 4;
-                        k0 = 8 * (cc & 3);
                     } else {  // NORMAL: partner dim d ^ 1 is in this thread
 #pragma unroll
                         for (int e = 0; e < 8; ++e) y[e] = x[e ^ 1];
-                        k0 = 4 * cc;
                     }
-                    float theta = rope_theta(rope, p, k0);
-                    float2 cs = rope_cs(rope, theta);
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
-                        if (rope.mode & 2) {
-                            if (e > 0) {
-                                theta = rope_next(rope, theta);
-                                cs = rope_cs(rope, theta);
-                            }
-                            x[e] = rope_rotate(x[e], y[e], cs, first);
-                        } else {
-                            if (e > 0 && (e & 1) == 0) {
-                                theta = rope_next(rope, theta);
-                                cs = rope_cs(rope, theta);
-                            }
-                            x[e] = rope_rotate(x[e], y[e], cs, (e & 1) == 0);
-                        }
+                        // pair k: NEOX d mod 32, NORMAL d / 2, with d = 8 cc + e; its (cos, sin) from lane k
+                        const int k = (rope.mode & 2) ? 8 * (cc & 3) + e : 4 * cc + (e >> 1);
+                        const float2 cs = make_float2(__shfl_sync(0xffffffffu, qcs.x, k), __shfl_sync(0xffffffffu, qcs.y, k));
+                        x[e] = rope_rotate(x[e], y[e], cs, (rope.mode & 2) ? first : (e & 1) == 0);
                     }
                 }
                 float am = 0.0f, part = 0.0f;
@@ -631,6 +620,10 @@ __global__ void __launch_bounds__(640, 1) decode_stream_kernel(const Args a) {
                 const uint8_t* kb = a.k_seq_ptrs ? reinterpret_cast<const uint8_t*>(a.k_seq_ptrs[seq]) : a.k_base + seq * a.k_nb2;
                 const uint8_t* vb = a.v_seq_ptrs ? reinterpret_cast<const uint8_t*>(a.v_seq_ptrs[seq]) : a.v_base + seq * a.v_nb2;
                 const int rr = len - 1 - p0;
+                // (cos, sin) of pair k = lane at position len - 1 (NEOX pairs element `lane` of
+                // both 32-element halves of a head; NORMAL takes pair d / 2 from its lane)
+                float2 kcs = make_float2(1.0f, 0.0f);
+                if (rope.n_dims > 0) kcs = rope_cs(rope, rope_theta(rope, len - 1, lane));
                 for (int gi = cw; gi < 8; gi += 4) {
                     const bool isv = gi >= 4;
                     const int g2 = gi & 3;
@@ -641,7 +634,8 @@ __global__ void __launch_bounds__(640, 1) decode_stream_kernel(const Args a) {
                         int k;
                         bool first;
                         const int pd = rope_pair(rope, d, k, first);
-                        xv = rope_rotate(xv, krow[pd], rope_cs(rope, rope_theta(rope, len - 1, k)), first);
+                        const float2 cs = make_float2(__shfl_sync(0xffffffffu, kcs.x, k), __shfl_sync(0xffffffffu, kcs.y, k));
+                        xv = rope_rotate(xv, krow[pd], cs, first);
                     }
                     if (!isv) {
                         quantize_block_warp<KT>(xv, Kraw + rr * rowK + g2 * GBK, lane);
