@@ -63,6 +63,31 @@ bool tensor_ok(const cvattn_tensor* t) {
     return true;
 }
 
+// Makes `device` current for the lifetime of the guard and restores the
+// caller's device afterwards, so a call made while another GPU is current
+// still runs on the context's device.
+class DeviceGuard {
+public:
+    explicit DeviceGuard(int device) {
+        if (cudaGetDevice(&prev_) != cudaSuccess) {
+            err_ = cudaErrorNoDevice;
+            return;
+        }
+        if (prev_ != device) err_ = cudaSetDevice(device);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (cudaGetDevice(&cur) == cudaSuccess && cur != prev_ && prev_ >= 0) cudaSetDevice(prev_);
+    }
+    cudaError_t error() const { return err_; }
+    DeviceGuard(const DeviceGuard&) = delete;
+    DeviceGuard& operator=(const DeviceGuard&) = delete;
+
+private:
+    int prev_ = -1;
+    cudaError_t err_ = cudaSuccess;
+};
+
 }  // namespace
 
 // ------------------------------------------------------------------ context
@@ -71,6 +96,9 @@ struct cvattn_context {
     int device;
     int* status;  // device word; 0 = clean
 };
+
+// The device of a context, for the entry points defined in other files.
+int cvattn_context_device(const cvattn_context* ctx) { return ctx ? ctx->device : -1; }
 
 extern "C" {
 
@@ -242,12 +270,15 @@ cvattn_status cvattn_context_create(int32_t device, cvattn_context** out) {
 
 void cvattn_context_destroy(cvattn_context* ctx) {
     if (!ctx) return;
+    DeviceGuard dg(ctx->device);
     cudaFree(ctx->status);
     delete ctx;
 }
 
 cvattn_status cvattn_context_sync_status(cvattn_context* ctx, void* stream, int32_t* detail) {
     if (!ctx) return CVATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard dg(ctx->device);
+    if (dg.error() != cudaSuccess) return from_cuda(dg.error());
     int v = 0;
     cudaError_t e = cudaMemcpyAsync(&v, ctx->status, sizeof(int), cudaMemcpyDeviceToHost, as_stream(stream));
     if (e == cudaSuccess) e = cudaStreamSynchronize(as_stream(stream));
@@ -269,6 +300,8 @@ cvattn_status cvattn_kv_append(cvattn_context* ctx, void* stream, const cvattn_t
     if (!src || !pos || (src_nb1 & 3) || (src_nb2 & 3) || (pos_nb1 & 3) || pos_nb1 < 0)
         return CVATTN_ERR_INVALID_ARGUMENT;
     if (reinterpret_cast<uintptr_t>(src) & 3) return CVATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard dg(ctx->device);
+    if (dg.error() != cudaSuccess) return from_cuda(dg.error());
     return from_cuda(launch_kv_append(as_stream(stream), *cache, src, src_nb1, src_nb2, pos, pos_nb1 / 4, n_new, batch,
                                       ctx->status));
 }
@@ -320,6 +353,8 @@ cvattn_status cvattn_kv_append_rope(cvattn_context* ctx, void* stream, const cva
     if (!src || !pos || (src_nb1 & 3) || (src_nb2 & 3) || (pos_nb1 & 3) || pos_nb1 < 0)
         return CVATTN_ERR_INVALID_ARGUMENT;
     if (reinterpret_cast<uintptr_t>(src) & 3) return CVATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard dg(ctx->device);
+    if (dg.error() != cudaSuccess) return from_cuda(dg.error());
     return from_cuda(launch_kv_append(as_stream(stream), *cache, src, src_nb1, src_nb2, pos, pos_nb1 / 4, n_new, batch,
                                       ctx->status, &d));
 }
@@ -328,6 +363,8 @@ cvattn_status cvattn_kv_dequantize(cvattn_context* ctx, void* stream, const cvat
                                    float* dst) {
     if (!ctx || !tensor_ok(cache) || n_rows < 0 || n_rows > cache->ne1 || (n_rows && !dst))
         return CVATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard dg(ctx->device);
+    if (dg.error() != cudaSuccess) return from_cuda(dg.error());
     return from_cuda(launch_kv_dequant(as_stream(stream), *cache, n_rows, dst));
 }
 
@@ -381,6 +418,8 @@ static cvattn_status decode_impl(cvattn_context* ctx, void* stream, const cvattn
         if (rope->unit_len != k.head_dim || rope->n_dims != k.head_dim || !decode_rope_supported(*p))
             return CVATTN_ERR_UNSUPPORTED;
     }
+    DeviceGuard dg(ctx->device);
+    if (dg.error() != cudaSuccess) return from_cuda(dg.error());
     if (p->max_kv_len == 0) {
         // nothing visible anywhere: ggml's S == 0 convention gives zeros
         for (int32_t s = 0; s < p->n_seq; ++s) {
@@ -428,6 +467,8 @@ cvattn_status cvattn_flash(cvattn_context* ctx, void* stream, const cvattn_flash
         for (int32_t i = 1; i < p->n_chunk_bounds; ++i)
             if (p->chunk_bounds[i] < p->chunk_bounds[i - 1]) return CVATTN_ERR_INVALID_ARGUMENT;
     }
+    DeviceGuard dg(ctx->device);
+    if (dg.error() != cudaSuccess) return from_cuda(dg.error());
     return from_cuda(launch_flash(as_stream(stream), *p, ctx->status));
 }
 
@@ -469,13 +510,21 @@ struct cvattn_kv_cache {
     uint32_t cur_len = 0;
     uint32_t view_len = 0;          // cur_len + rows appended by the last update
     int cur_slot = 0;
-    // offloaded host slots (src/cosyvoice-kv-cache.cpp:19-32)
+    // offloaded host slots (src/cosyvoice-kv-cache.cpp:19-32), in pinned memory so
+    // the copies run asynchronously; `done` marks the end of the last copy that
+    // touched the slot (later copies on another stream wait for it, and the host
+    // waits for it before it reads, resizes or frees the buffer)
     struct host_slot {
         uint32_t len = 0;
-        std::vector<char> buffer;
+        char* buffer = nullptr;
+        size_t bytes = 0;           // bytes holding len positions of every layer
+        size_t capacity = 0;
+        cudaEvent_t done = nullptr;
+        bool pending = false;       // `done` was recorded and may not have completed
     };
     std::vector<host_slot> offloaded;
-    // decode scratch, grown on demand
+    // decode workspace, sized at creation for the largest supported query-head
+    // count (8 per KV head) and max_seq positions: the attention call never allocates
     void* ws = nullptr;
     size_t ws_bytes = 0;
     int32_t* d_len = nullptr;       // device kv lengths [batch]
@@ -497,16 +546,65 @@ static cvattn_tensor cache_tensor(const cvattn_kv_cache* c, int layer, int slot,
     return t;
 }
 
+// Waits for the copies that last touched a host slot (host side).
+static cudaError_t host_slot_wait(cvattn_kv_cache::host_slot& hs) {
+    if (!hs.pending) return cudaSuccess;
+    cudaError_t e = cudaEventSynchronize(hs.done);
+    if (e == cudaSuccess) hs.pending = false;
+    return e;
+}
+
+static void host_slot_free(cvattn_kv_cache::host_slot& hs) {
+    host_slot_wait(hs);
+    if (hs.buffer) cudaFreeHost(hs.buffer);
+    hs.buffer = nullptr;
+    hs.capacity = hs.bytes = 0;
+    hs.len = 0;
+}
+
+// Host bytes of one offloaded slot holding n positions: per layer K for every
+// batch entry, then V (src/cosyvoice-kv-cache.cpp:153-172).
+static size_t host_slot_bytes(const cvattn_kv_cache* c, uint32_t n) {
+    return ((size_t)c->k_nb1 + (size_t)c->v_nb1) * n * (size_t)c->p.batch * (size_t)c->p.layers;
+}
+
+// Copies positions [0, n) of every batch entry of t to or from host, where the
+// host rows of batch entry b start at host + b * n * t.nb1: one strided copy
+// covers the whole batch.
+static cudaError_t copy_rows_2d(cudaStream_t s, const cvattn_tensor& t, uint32_t n, char* host, bool to_host) {
+    const size_t w = (size_t)t.nb1 * n;
+    if (!w) return cudaSuccess;
+    if (to_host)
+        return cudaMemcpy2DAsync(host, w, t.data, (size_t)t.nb2, w, (size_t)t.ne2, cudaMemcpyDeviceToHost, s);
+    return cudaMemcpy2DAsync(t.data, (size_t)t.nb2, host, w, w, (size_t)t.ne2, cudaMemcpyHostToDevice, s);
+}
+
 extern "C" {
+
+void cvattn_kv_cache_destroy(cvattn_kv_cache* c) {
+    if (!c) return;
+    DeviceGuard dg(c->ctx->device);
+    for (auto& hs : c->offloaded) {
+        host_slot_free(hs);
+        if (hs.done) cudaEventDestroy(hs.done);
+    }
+    cudaFree(c->base);
+    cudaFree(c->d_len);
+    if (c->ws) cudaFree(c->ws);
+    delete c;
+}
 
 cvattn_status cvattn_kv_cache_create(cvattn_context* ctx, const cvattn_kv_cache_params* p, cvattn_kv_cache** out) {
     if (!ctx || !p || !out) return CVATTN_ERR_INVALID_ARGUMENT;
     *out = nullptr;
     if (p->layers <= 0 || p->n_kv_heads <= 0 || p->k_head_dim <= 0 || p->v_head_dim <= 0 || p->max_seq == 0 ||
-        p->batch <= 0 || p->n_slots <= 0 || p->n_offloaded_slots < 0 || !known_type(p->k_type) || !known_type(p->v_type))
+        p->max_seq > 0x7fffffffu || p->batch <= 0 || p->n_slots <= 0 || p->n_offloaded_slots < 0 ||
+        !known_type(p->k_type) || !known_type(p->v_type))
         return CVATTN_ERR_INVALID_ARGUMENT;
     const int64_t ke = (int64_t)p->k_head_dim * p->n_kv_heads, ve = (int64_t)p->v_head_dim * p->n_kv_heads;
     if (ke % 32 || ve % 32) return CVATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard dg(ctx->device);
+    if (dg.error() != cudaSuccess) return from_cuda(dg.error());
     cvattn_kv_cache* c = new (std::nothrow) cvattn_kv_cache();
     if (!c) return CVATTN_ERR_ALLOC;
     c->ctx = ctx;
@@ -526,25 +624,28 @@ cvattn_status cvattn_kv_cache_create(cvattn_context* ctx, const cvattn_kv_cache_
         off += vb;
     }
     c->bytes = off;
-    cudaError_t e = cudaSetDevice(ctx->device);
-    if (e == cudaSuccess) e = cudaMalloc(&c->base, off);
+    c->offloaded.resize(p->n_offloaded_slots);
+    cudaError_t e = cudaMalloc(&c->base, off);
     if (e == cudaSuccess) e = cudaMalloc(&c->d_len, sizeof(int32_t) * p->batch);
+    // the decode workspace for the largest query-head count the engine supports
+    if (e == cudaSuccess && p->k_head_dim == p->v_head_dim &&
+        decode_supported(p->k_type, p->v_type, p->k_head_dim, 8 * p->n_kv_heads, p->n_kv_heads)) {
+        const size_t need = decode_workspace_bytes(p->k_type, p->v_type, p->batch, (int)p->max_seq,
+                                                   8 * p->n_kv_heads, p->n_kv_heads, p->k_head_dim);
+        e = cudaMalloc(&c->ws, need);
+        if (e == cudaSuccess) {
+            c->ws_bytes = need;
+            e = cudaMemset(c->ws, 0, need);
+        }
+    }
+    for (auto& hs : c->offloaded)
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&hs.done, cudaEventDisableTiming);
     if (e != cudaSuccess) {
-        if (c->base) cudaFree(c->base);
-        delete c;
+        cvattn_kv_cache_destroy(c);
         return from_cuda(e);
     }
-    c->offloaded.resize(p->n_offloaded_slots);
     *out = c;
     return CVATTN_OK;
-}
-
-void cvattn_kv_cache_destroy(cvattn_kv_cache* c) {
-    if (!c) return;
-    cudaFree(c->base);
-    cudaFree(c->d_len);
-    if (c->ws) cudaFree(c->ws);
-    delete c;
 }
 
 cvattn_status cvattn_kv_cache_tensor(cvattn_kv_cache* c, int32_t layer, int32_t slot, int32_t which,
@@ -587,7 +688,7 @@ cvattn_status cvattn_kv_cache_attention(cvattn_kv_cache* c, void* stream, int32_
     const cvattn_tensor vt = cache_tensor(c, layer, c->cur_slot, 1);
     const int32_t n_kv = (int32_t)c->view_len;
     const int64_t D = kt.head_dim;
-    if (n_q == 1 && mask_mode == CVATTN_MASK_NONE &&
+    if (n_q == 1 && mask_mode == CVATTN_MASK_NONE && n_kv > 0 && c->ws &&
         decode_supported(kt.type, vt.type, kt.head_dim, n_q_heads, kt.n_heads)) {
         cvattn_decode_params dp{};
         dp.q = q;
@@ -600,29 +701,19 @@ cvattn_status cvattn_kv_cache_attention(cvattn_kv_cache* c, void* stream, int32_
         dp.n_q_heads = n_q_heads;
         dp.max_kv_len = n_kv;
         dp.scale = 1.0f / std::sqrt((float)D);
-        const size_t need =
-            decode_workspace_bytes(kt.type, vt.type, c->p.batch, (int)c->p.max_seq, n_q_heads, kt.n_heads, (int)D);
-        if (need == 0) return CVATTN_ERR_UNSUPPORTED;
-        if (c->ws_bytes < need) {
-            if (c->ws) cudaFree(c->ws);
-            c->ws = nullptr;
-            c->ws_bytes = 0;
-            cudaError_t e = cudaMalloc(&c->ws, need);
-            if (e != cudaSuccess) return from_cuda(e);
-            c->ws_bytes = need;
-            e = cudaMemsetAsync(c->ws, 0, need, as_stream(stream));
-            if (e != cudaSuccess) return from_cuda(e);
-        }
-        std::vector<int32_t> lens(c->p.batch, n_kv);
-        cudaError_t e = cudaMemcpyAsync(c->d_len, lens.data(), sizeof(int32_t) * lens.size(), cudaMemcpyHostToDevice,
-                                        as_stream(stream));
-        if (e != cudaSuccess) return from_cuda(e);
-        // the pageable source must stay valid until the copy has been staged
-        e = cudaStreamSynchronize(as_stream(stream));
-        if (e != cudaSuccess) return from_cuda(e);
-        dp.kv_len = c->d_len;
         dp.workspace = c->ws;
         dp.workspace_size = c->ws_bytes;
+        dp.kv_len = c->d_len;
+        // the view length goes to the device with a tiny kernel (no host buffer, no
+        // synchronization, capturable); the same launch clears the ticket counters,
+        // so a decode that gave up on an earlier call cannot leave them stale
+        {
+            DeviceGuard dg(c->ctx->device);
+            if (dg.error() != cudaSuccess) return from_cuda(dg.error());
+            cudaError_t e = launch_fill_lengths(as_stream(stream), c->d_len, c->p.batch, n_kv,
+                                                static_cast<uint32_t*>(c->ws), c->p.batch);
+            if (e != cudaSuccess) return from_cuda(e);
+        }
         return cvattn_decode(c->ctx, stream, &dp);
     }
     cvattn_flash_params fp{};
@@ -668,56 +759,93 @@ int32_t cvattn_kv_cache_current_slot(const cvattn_kv_cache* c) { return c ? c->c
 cvattn_status cvattn_kv_cache_offload_slot(cvattn_kv_cache* c, void* stream, int32_t slot_idx, uint32_t n_tokens) {
     if (!c || slot_idx < 0 || slot_idx >= (int32_t)c->offloaded.size() || n_tokens > c->p.max_seq)
         return CVATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard dg(c->ctx->device);
+    if (dg.error() != cudaSuccess) return from_cuda(dg.error());
     auto& hs = c->offloaded[slot_idx];
+    const cudaStream_t s = as_stream(stream);
+    const size_t need = host_slot_bytes(c, n_tokens);
+    cudaError_t e = cudaSuccess;
+    if (need > hs.capacity) {  // grow: the old buffer may still be read by an earlier load
+        host_slot_free(hs);
+        e = cudaHostAlloc(reinterpret_cast<void**>(&hs.buffer), need, cudaHostAllocDefault);
+        if (e != cudaSuccess) {
+            hs.buffer = nullptr;
+            return from_cuda(e);
+        }
+        hs.capacity = need;
+    } else if (hs.pending) {  // an earlier load from this buffer must finish before it is overwritten
+        e = cudaStreamWaitEvent(s, hs.done, 0);
+        if (e != cudaSuccess) return from_cuda(e);
+    }
+    hs.len = n_tokens;
+    hs.bytes = need;
     const size_t kn = (size_t)c->k_nb1 * n_tokens, vn = (size_t)c->v_nb1 * n_tokens;
     const size_t per_layer = (kn + vn) * c->p.batch;
-    hs.buffer.resize(per_layer * c->p.layers);
-    hs.len = n_tokens;
-    for (int l = 0; l < c->p.layers; ++l) {  // layout of kv-cache.cpp:160-172
-        char* kdst = hs.buffer.data() + l * per_layer;
+    // offload_cache reads kv_cache_layers[i], the layers of device slot 0, which every
+    // offloadable step shares (src/cosyvoice-kv-cache.cpp:163-172; token2wav binds slot
+    // 0 for offload steps, src/cosyvoice-token2wav.cpp:390)
+    for (int l = 0; l < c->p.layers && e == cudaSuccess; ++l) {
+        char* kdst = hs.buffer + (size_t)l * per_layer;
         char* vdst = kdst + kn * c->p.batch;
-        const cvattn_tensor kt = cache_tensor(c, l, c->cur_slot, 0);
-        const cvattn_tensor vt = cache_tensor(c, l, c->cur_slot, 1);
-        cvattn_status s = cvattn_kv_copy_to_host(stream, &kt, (int32_t)n_tokens, kdst);
-        if (s == CVATTN_OK) s = cvattn_kv_copy_to_host(stream, &vt, (int32_t)n_tokens, vdst);
-        if (s != CVATTN_OK) return s;
+        e = copy_rows_2d(s, cache_tensor(c, l, 0, 0), n_tokens, kdst, true);
+        if (e == cudaSuccess) e = copy_rows_2d(s, cache_tensor(c, l, 0, 1), n_tokens, vdst, true);
     }
-    return from_cuda(cudaStreamSynchronize(as_stream(stream)));
+    if (e == cudaSuccess) e = cudaEventRecord(hs.done, s);
+    if (e == cudaSuccess) hs.pending = true;
+    return from_cuda(e);
 }
 
 cvattn_status cvattn_kv_cache_load_slot(cvattn_kv_cache* c, void* stream, int32_t slot_idx) {
     if (!c || slot_idx < 0 || slot_idx >= (int32_t)c->offloaded.size()) return CVATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard dg(c->ctx->device);
+    if (dg.error() != cudaSuccess) return from_cuda(dg.error());
     auto& hs = c->offloaded[slot_idx];
     c->cur_len = hs.len;
     c->view_len = hs.len;
     if (hs.len == 0) return CVATTN_OK;
+    const cudaStream_t s = as_stream(stream);
+    cudaError_t e = cudaSuccess;
+    if (hs.pending) e = cudaStreamWaitEvent(s, hs.done, 0);  // the offload may run on another stream
     const size_t kn = (size_t)c->k_nb1 * hs.len, vn = (size_t)c->v_nb1 * hs.len;
     const size_t per_layer = (kn + vn) * c->p.batch;
-    for (int l = 0; l < c->p.layers; ++l) {
-        const char* ksrc = hs.buffer.data() + l * per_layer;
-        const char* vsrc = ksrc + kn * c->p.batch;
-        const cvattn_tensor kt = cache_tensor(c, l, c->cur_slot, 0);
-        const cvattn_tensor vt = cache_tensor(c, l, c->cur_slot, 1);
-        cvattn_status s = cvattn_kv_copy_from_host(stream, &kt, (int32_t)hs.len, ksrc);
-        if (s == CVATTN_OK) s = cvattn_kv_copy_from_host(stream, &vt, (int32_t)hs.len, vsrc);
-        if (s != CVATTN_OK) return s;
+    // load_cache writes kv_cache_layers[i + cur_slot_idx * layers] (src/cosyvoice-kv-cache.cpp:233-243)
+    for (int l = 0; l < c->p.layers && e == cudaSuccess; ++l) {
+        char* ksrc = hs.buffer + (size_t)l * per_layer;
+        char* vsrc = ksrc + kn * c->p.batch;
+        e = copy_rows_2d(s, cache_tensor(c, l, c->cur_slot, 0), hs.len, ksrc, false);
+        if (e == cudaSuccess) e = copy_rows_2d(s, cache_tensor(c, l, c->cur_slot, 1), hs.len, vsrc, false);
     }
-    return from_cuda(cudaStreamSynchronize(as_stream(stream)));
+    if (e == cudaSuccess) e = cudaEventRecord(hs.done, s);
+    if (e == cudaSuccess) hs.pending = true;
+    return from_cuda(e);
+}
+
+cvattn_status cvattn_kv_cache_offloaded_slot(cvattn_kv_cache* c, int32_t slot_idx, const void** data, size_t* bytes,
+                                             uint32_t* n_tokens) {
+    if (!c || slot_idx < 0 || slot_idx >= (int32_t)c->offloaded.size() || !data || !bytes)
+        return CVATTN_ERR_INVALID_ARGUMENT;
+    auto& hs = c->offloaded[slot_idx];
+    DeviceGuard dg(c->ctx->device);
+    if (dg.error() != cudaSuccess) return from_cuda(dg.error());
+    cudaError_t e = host_slot_wait(hs);
+    if (e != cudaSuccess) return from_cuda(e);
+    *data = hs.buffer;
+    *bytes = hs.bytes;
+    if (n_tokens) *n_tokens = hs.len;
+    return CVATTN_OK;
 }
 
 size_t cvattn_kv_cache_offloaded_size(const cvattn_kv_cache* c) {
     if (!c) return 0;
     size_t n = 0;
-    for (const auto& s : c->offloaded) n += s.buffer.capacity();
+    for (const auto& s : c->offloaded) n += s.capacity;
     return n;
 }
 
 void cvattn_kv_cache_clear_offloaded(cvattn_kv_cache* c) {
     if (!c) return;
-    for (auto& s : c->offloaded) {
-        std::vector<char>().swap(s.buffer);
-        s.len = 0;
-    }
+    DeviceGuard dg(c->ctx->device);
+    for (auto& s : c->offloaded) host_slot_free(s);
 }
 
 // ------------------------------------------------------------- DiT plan

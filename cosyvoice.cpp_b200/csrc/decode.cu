@@ -107,12 +107,7 @@ cudaError_t launch_decode(cudaStream_t stream, const cvattn_decode_params& p, in
         a.ws_ml = reinterpret_cast<float*>(ws + cnt_bytes);
         a.ws_o = reinterpret_cast<float*>(ws + cnt_bytes + align256((size_t)p.n_seq * chunks_tc * p.n_q_heads * 2 * 4));
         // persistent pipelined kernel when its ring of stages fits one SM
-        static int num_sms = 0;
-        if (num_sms == 0) {
-            int dev = 0;
-            cudaGetDevice(&dev);
-            cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
-        }
+        const int num_sms = current_sm_count();
         const bool persistent = !(p.flags & CVATTN_DECODE_NOT_PERSISTENT) && num_sms > 0;
         if (persistent && !(p.flags & CVATTN_DECODE_WIDE_CHUNKS) && dstream::supported_type(p.k.type) &&
             dstream::supported_type(p.v.type) && p.n_seq <= dstream::kMaxSeq &&

@@ -36,17 +36,19 @@ constexpr int kMaxDevices = 64;
 void* g_scratch_addr[kMaxDevices] = {};
 std::mutex g_setup_mutex;
 
-// Device address of the scratch on the current device, looked up once per
-// device (the first call made while that device is current).
-cudaError_t scratch_address(void** out) {
-    int dev = -1;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
+// Device address of the scratch on `dev`, looked up once per device with that
+// device current (the caller's device is restored afterwards).
+cudaError_t scratch_address(int dev, void** out) {
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lock(g_setup_mutex);
     if (!g_scratch_addr[dev]) {
+        int prev = -1;
+        cudaError_t e = cudaGetDevice(&prev);
+        if (e != cudaSuccess) return e;
+        if (prev != dev && (e = cudaSetDevice(dev)) != cudaSuccess) return e;
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_decode_scratch);
+        if (prev != dev) cudaSetDevice(prev);
         if (e != cudaSuccess) return e;
         g_scratch_addr[dev] = p;
     }
@@ -56,19 +58,31 @@ cudaError_t scratch_address(void** out) {
 
 }  // namespace
 
+// The device of a context (capi.cpp).
+int cvattn_context_device(const cvattn_context* ctx);
+
 extern "C" cvattn_status cvattn_decode_noalloc(cvattn_context* ctx, void* stream, const cvattn_decode_params* p) {
-    if (!ctx || !p) return CVATTN_ERR_INVALID_ARGUMENT;
-    if (p->n_seq <= 0) return p->n_seq == 0 ? CVATTN_OK : CVATTN_ERR_INVALID_ARGUMENT;
+    // the same argument checks as cvattn_decode, before the workspace size is asked,
+    // so both entry points give the same status for the same bad parameters
+    if (!ctx || !p || !p->q || !p->out || !p->kv_len) return CVATTN_ERR_INVALID_ARGUMENT;
+    if (p->n_seq < 0 || p->max_kv_len < 0 || p->n_q_heads <= 0) return CVATTN_ERR_INVALID_ARGUMENT;
+    if (p->n_seq == 0) return CVATTN_OK;
     const size_t need = cvattn_decode_workspace_size(p->k.type, p->v.type, p->n_seq, p->max_kv_len, p->n_q_heads,
                                                      p->k.n_heads, p->k.head_dim);
     if (need == 0) return CVATTN_ERR_UNSUPPORTED;
     if (need > kScratchBytes) return CVATTN_ERR_LENGTH;  // beyond the static scratch: nothing launched
+    const int dev = cvattn_context_device(ctx);
     void* scratch = nullptr;
-    cudaError_t e = scratch_address(&scratch);
+    cudaError_t e = scratch_address(dev, &scratch);
     if (e != cudaSuccess) return CVATTN_ERR_CUDA;
-    // the per-sequence ticket counters lead the workspace (256-byte aligned block)
+    // the per-sequence ticket counters lead the workspace (256-byte aligned block);
+    // cleared with the context's device current
+    int prev = -1;
+    if (cudaGetDevice(&prev) != cudaSuccess) return CVATTN_ERR_CUDA;
+    if (prev != dev && cudaSetDevice(dev) != cudaSuccess) return CVATTN_ERR_CUDA;
     const size_t counter_bytes = ((size_t)p->n_seq * 4 + 255) & ~size_t(255);
     e = cudaMemsetAsync(scratch, 0, counter_bytes, reinterpret_cast<cudaStream_t>(stream));
+    if (prev != dev) cudaSetDevice(prev);
     if (e != cudaSuccess) return CVATTN_ERR_CUDA;
     cvattn_decode_params q = *p;
     q.workspace = scratch;

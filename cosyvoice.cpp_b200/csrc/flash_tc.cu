@@ -108,12 +108,8 @@ cudaError_t launch_flash(cudaStream_t stream, const cvattn_flash_params& a, int*
     }
     if (!(a.flags & CVATTN_FLASH_ONE_TILE)) {
         // persistent kernel: one CTA per SM over the query-tile pairs
-        static int num_sms = 0;
-        if (num_sms == 0) {
-            int dev = 0;
-            cudaGetDevice(&dev);
-            cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
-        }
+        const int num_sms = current_sm_count();
+        if (num_sms <= 0) return cudaErrorInvalidDevice;
         const long n_qt = (a.n_q + BM - 1) / BM;
         const long items = p.G >= 2 ? n_qt * a.batch * (a.n_q_heads / p.G) * ((p.G + 1) / 2)
                                     : ((n_qt + 1) / 2) * a.batch * a.n_q_heads;

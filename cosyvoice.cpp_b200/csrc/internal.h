@@ -24,6 +24,15 @@ cudaError_t launch_rope(cudaStream_t stream, const RopeDev& rope, const float* x
                         int64_t out_nb1f, const int32_t* pos, int n_rows, int row_len);
 cudaError_t launch_kv_dequant(cudaStream_t stream, const cvattn_tensor& cache, int n_rows, float* dst);
 
+// kv_append.cu: per-device SM count (looked up once per device, thread-safe)
+int device_sm_count(int device);
+// The current device's SM count (0 if the runtime cannot say).
+int current_sm_count();
+// Fill n int32 lengths with one value and zero n_tickets 32-bit ticket counters
+// (one launch; either count may be 0).
+cudaError_t launch_fill_lengths(cudaStream_t stream, int32_t* lens, int n, int32_t value, uint32_t* tickets,
+                                int n_tickets);
+
 // decode.cu
 int decode_chunk_positions(int k_type, int v_type, int n_kv_heads, int head_dim);
 size_t decode_workspace_bytes(int k_type, int v_type, int n_seq, int max_kv_len, int n_q_heads, int n_kv_heads, int head_dim);

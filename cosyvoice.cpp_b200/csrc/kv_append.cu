@@ -10,6 +10,8 @@
 // With a RoPE the K rows are rotated on the way in, as ggml_rope_ext does
 // before update_cache (src/cosyvoice-llm.cpp:57,180; src/cosyvoice-graph.cpp:355);
 // the standalone rope kernel covers Q and other callers.
+#include <atomic>
+
 #include "common.cuh"
 #include "internal.h"
 #include "rope.cuh"
@@ -147,6 +149,46 @@ cudaError_t launch_kv_dequant(cudaStream_t stream, const cvattn_tensor& c, int n
     default: return cudaErrorInvalidValue;
     }
 #undef CVATTN_DEQ_CASE
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------- per-device state
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::atomic<int> g_sm_count[kMaxDevices];  // 0 = not looked up yet
+}  // namespace
+
+int device_sm_count(int device) {
+    if (device < 0 || device >= kMaxDevices) return 0;
+    int n = g_sm_count[device].load(std::memory_order_relaxed);
+    if (n == 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+        g_sm_count[device].store(n, std::memory_order_relaxed);
+    }
+    return n;
+}
+
+int current_sm_count() {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    return device_sm_count(dev);
+}
+
+// ------------------------------------------------- lengths and tickets
+
+__global__ void fill_lengths_kernel(int32_t* __restrict__ lens, int n, int32_t value, uint32_t* __restrict__ tickets,
+                                    int n_tickets) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) lens[i] = value;
+    if (i < n_tickets) tickets[i] = 0u;
+}
+
+cudaError_t launch_fill_lengths(cudaStream_t stream, int32_t* lens, int n, int32_t value, uint32_t* tickets,
+                                int n_tickets) {
+    const int m = n > n_tickets ? n : n_tickets;
+    if (m <= 0) return cudaSuccess;
+    fill_lengths_kernel<<<(m + 255) / 256, 256, 0, stream>>>(lens, n, value, tickets, n_tickets);
     return cudaGetLastError();
 }
 

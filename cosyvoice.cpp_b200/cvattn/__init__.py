@@ -367,6 +367,17 @@ class KVCache:
     def load_slot(self, idx: int, stream=None) -> None:
         check(lib.cvattn_kv_cache_load_slot(self.handle, _stream(stream), idx), "load_slot")
 
+    def offloaded_slot(self, idx: int):
+        """(bytes of host slot idx as a numpy uint8 copy, its length in positions), once its copies completed."""
+        import numpy as np
+        data, nbytes, n = ctypes.c_void_p(), ctypes.c_size_t(), ctypes.c_uint32()
+        check(lib.cvattn_kv_cache_offloaded_slot(self.handle, idx, ctypes.byref(data), ctypes.byref(nbytes),
+                                                 ctypes.byref(n)), "offloaded_slot")
+        if not nbytes.value:
+            return np.zeros(0, np.uint8), int(n.value)
+        buf = (ctypes.c_uint8 * nbytes.value).from_address(data.value)
+        return np.frombuffer(buf, dtype=np.uint8).copy(), int(n.value)
+
     @property
     def offloaded_size(self) -> int:
         return int(lib.cvattn_kv_cache_offloaded_size(self.handle))

@@ -121,6 +121,7 @@ SIGNATURES = [
     ("cvattn_kv_cache_current_slot", c_int32, [c_void_p]),
     ("cvattn_kv_cache_offload_slot", c_int32, [c_void_p, c_void_p, c_int32, c_uint32]),
     ("cvattn_kv_cache_load_slot", c_int32, [c_void_p, c_void_p, c_int32]),
+    ("cvattn_kv_cache_offloaded_slot", c_int32, [c_void_p, c_int32, P(c_void_p), P(c_size_t), P(c_uint32)]),
     ("cvattn_kv_cache_offloaded_size", c_size_t, [c_void_p]),
     ("cvattn_kv_cache_clear_offloaded", None, [c_void_p]),
     ("cvattn_dit_sched_plan", c_int32,

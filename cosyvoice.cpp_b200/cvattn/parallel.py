@@ -88,7 +88,14 @@ class SplitKVDecode:
 
     def __call__(self, q):
         cv = self.cv
-        self.cv.decode(self.ctx, q.reshape(1, self.hq, self.d), self.k, self.v, self.kv_len, max(self.count, 1),
-                       out=self.po, emit_partial=True, partial_ml=self.pml)
+        if self.count > 0:
+            self.cv.decode(self.ctx, q.reshape(1, self.hq, self.d), self.k, self.v, self.kv_len, self.count,
+                           out=self.po, emit_partial=True, partial_ml=self.pml)
+        else:
+            # an empty slice (a sequence shorter than align * world) still joins the
+            # gather, with the partial the combine skips: max -inf, sum 0
+            self.po.zero_()
+            self.pml[..., 0] = float("-inf")
+            self.pml[..., 1] = 0.0
         po, pml = gather_partials(self.po[0], self.pml[0], self.group)
         return cv.combine(po, pml)

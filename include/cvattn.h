@@ -239,7 +239,12 @@ typedef struct cvattn_decode_params {
 size_t cvattn_decode_workspace_size(int32_t k_type, int32_t v_type, int32_t n_seq, int32_t max_kv_len,
                                     int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim);
 
-/* Zero a workspace (once, after allocation).  The kernels leave it zeroed. */
+/* Zero a workspace: once after allocation, and again after
+ * cvattn_context_sync_status has reported CVATTN_ERR_TIMEOUT or
+ * CVATTN_ERR_DEVICE for a decode that used it.  A completed decode leaves its
+ * ticket counters at zero; a decode whose kernel gave up early can leave them
+ * counting, and later decodes through that workspace would then not merge
+ * their split partials. */
 cvattn_status cvattn_workspace_init(void* stream, void* workspace, size_t bytes);
 
 cvattn_status cvattn_decode(cvattn_context* ctx, void* stream, const cvattn_decode_params* p);
@@ -385,7 +390,10 @@ cvattn_status cvattn_kv_cache_update(cvattn_kv_cache* c, void* stream, int32_t l
 /* attention_forward (src/cosyvoice-kv-cache.cpp:379-386) over the current view
  * of (layer, bound slot).  q f32 [batch][n_q][n_q_heads][head_dim]; scale
  * 1/sqrt(head_dim); n_q == 1 without a mask runs the decode kernel, anything
- * else the tensor-core flash kernel.  mask semantics as cvattn_flash_params. */
+ * else the tensor-core flash kernel.  mask semantics as cvattn_flash_params.
+ * The call neither allocates nor synchronizes: the decode workspace is sized
+ * at creation, and the view length reaches the device through a small kernel
+ * on the stream (which also clears the workspace's ticket counters). */
 cvattn_status cvattn_kv_cache_attention(cvattn_kv_cache* c, void* stream, int32_t layer,
                                         const float* q, int32_t n_q, int32_t n_q_heads,
                                         int32_t mask_mode, const uint16_t* mask, int64_t mask_nb1,
@@ -399,13 +407,28 @@ int32_t       cvattn_kv_cache_bind_slot(cvattn_kv_cache* c, int32_t slot);
 cvattn_status cvattn_kv_cache_slide_slot(cvattn_kv_cache* c);
 int32_t       cvattn_kv_cache_current_slot(const cvattn_kv_cache* c);
 
-/* offload_slot / load_slot (src/cosyvoice-kv-cache.cpp:148-246,276-290):
- * positions [0, n_tokens) of every layer of the bound slot to host slot
- * `offloaded_slot` and back (load restores cur_len).  Synchronous on the
- * stream, like the reference's ggml_backend_sched_synchronize. */
+/* offload_slot / load_slot (src/cosyvoice-kv-cache.cpp:148-246,276-290).
+ * offload copies positions [0, n_tokens) of every layer of device slot 0 --
+ * the slot the reference's offload_cache reads (kv_cache_layers[i], :163-172),
+ * which every offloadable DiT step binds (src/cosyvoice-token2wav.cpp:390) --
+ * to host slot `offloaded_slot`; load copies a host slot into the bound
+ * device slot (:233-243) and sets cur_len to its length.  The host layout is
+ * the reference's: per layer, K of every batch entry, then V.
+ * Unlike the reference, which synchronizes after every transfer, both calls
+ * only enqueue copies on the stream (one strided copy per layer and tensor,
+ * from or into pinned host memory) and return, so the copies overlap the next
+ * step's kernels.  Stream order covers later kernels on the same stream; a
+ * load or offload on another stream first waits for the slot's last copy. */
 cvattn_status cvattn_kv_cache_offload_slot(cvattn_kv_cache* c, void* stream, int32_t offloaded_slot,
                                            uint32_t n_tokens);
 cvattn_status cvattn_kv_cache_load_slot(cvattn_kv_cache* c, void* stream, int32_t offloaded_slot);
+/* The bytes of host slot `offloaded_slot` (struct offloaded_kv_cache's buffer
+ * and len, src/cosyvoice-kv-cache.cpp:19-32): waits on the host until the
+ * slot's last copy has completed, then returns its address, its byte count
+ * and (optional) its length in positions.  The pointer stays valid until the
+ * slot grows, is cleared or the cache is destroyed. */
+cvattn_status cvattn_kv_cache_offloaded_slot(cvattn_kv_cache* c, int32_t offloaded_slot, const void** data,
+                                             size_t* bytes, uint32_t* n_tokens);
 size_t        cvattn_kv_cache_offloaded_size(const cvattn_kv_cache* c);
 void          cvattn_kv_cache_clear_offloaded(cvattn_kv_cache* c);
 

@@ -23,7 +23,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, result_q):
+def _worker(rank, world, port, result_q, L=5000):
     import datetime
     import sys
     import torch
@@ -40,16 +40,17 @@ def _worker(rank, world, port, result_q):
         from oracle import oracle as O
         ctx = cv.Context(rank)
         rng = np.random.default_rng(5)
-        L, Hq, Hkv, D = 5000, 14, 2, 64
+        Hq, Hkv, D = 14, 2, 64
         kx = rng.standard_normal((L, Hkv * D)).astype(np.float32)
         vx = rng.standard_normal((L, Hkv * D)).astype(np.float32)
         q = rng.standard_normal((Hq, D)).astype(np.float32)
         kq, vq = O.quantize(O.Q8_0, kx), O.quantize(O.Q4_0, vx)
         start, count = split_positions(L, world)[rank]
-        kbuf = torch.tensor(kq[start:start + count].reshape(-1), device="cuda")
-        vbuf = torch.tensor(vq[start:start + count].reshape(-1), device="cuda")
-        kd = cv.kv_tensor(kbuf, cv.Q8_0, Hkv, D, count, 1)
-        vd = cv.kv_tensor(vbuf, cv.Q4_0, Hkv, D, count, 1)
+        # an empty slice (L < 128 * world) keeps a one-row buffer: SplitKVDecode skips its decode
+        kbuf = torch.tensor(kq[start:start + max(count, 1)].reshape(-1), device="cuda")
+        vbuf = torch.tensor(vq[start:start + max(count, 1)].reshape(-1), device="cuda")
+        kd = cv.kv_tensor(kbuf, cv.Q8_0, Hkv, D, max(count, 1), 1)
+        vd = cv.kv_tensor(vbuf, cv.Q4_0, Hkv, D, max(count, 1), 1)
         dec = SplitKVDecode(ctx, kd, vd, count, Hq, D)
         out = dec(torch.tensor(q, device="cuda")).cpu().numpy()
         torch.cuda.synchronize()
@@ -64,7 +65,9 @@ def _worker(rank, world, port, result_q):
         dist.destroy_process_group()
 
 
-def test_split_kv_decode_two_gpus():
+@pytest.mark.parametrize("L", [5000, 100])
+def test_split_kv_decode_two_gpus(L):
+    """L = 100 leaves rank 1 an empty slice: it must still join the gather."""
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -72,7 +75,7 @@ def test_split_kv_decode_two_gpus():
     mpc = mp.get_context("spawn")
     q = mpc.Queue()
     port = _free_port()
-    procs = [mpc.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [mpc.Process(target=_worker, args=(r, 2, port, q, L)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in procs)

@@ -85,6 +85,24 @@ def _worker(rank, world, port, result_q):
         full_o, full_ml = _partials(q, k, v, 0.125)
         full = full_o / full_ml[:, 1:2]
         err = float(np.abs(merged - full).max())
+
+        # --- a sequence shorter than 128 * world: the trailing rank's slice is empty;
+        # it still joins the gather with the partial the merge skips (max -inf, sum 0)
+        Ls = 100
+        start, count = split_positions(Ls, world)[rank]
+        assert (count == 0) == (rank > 0)
+        if count:
+            o, ml = _partials(q, k[start:start + count], v[start:start + count], 0.125)
+        else:
+            o = np.zeros((Hq, D), np.float32)
+            ml = np.tile(np.array([-np.inf, 0.0], np.float32), (Hq, 1))
+        po, pml = gather_partials(torch.from_numpy(o), torch.from_numpy(ml))
+        po, pml = po.numpy(), pml.numpy()
+        M = pml[:, :, 0].max(axis=0)
+        w = np.where(np.isinf(pml[:, :, 0]), 0.0, np.exp2(pml[:, :, 0] - M))
+        merged = (w[:, :, None] * po).sum(0) / (w * pml[:, :, 1]).sum(0)[:, None]
+        full_o, full_ml = _partials(q, k[:Ls], v[:Ls], 0.125)
+        err = max(err, float(np.abs(merged - full_o / full_ml[:, 1:2]).max()))
         result_q.put((rank, union, loads, err))
     finally:
         dist.destroy_process_group()
