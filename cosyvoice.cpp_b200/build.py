@@ -40,10 +40,10 @@ def _units():
         units.append((os.path.join(CSRC, src), obj, []))
     for name, tid in K_TYPES.items():
         for stem in ("decode_inst", "flash_inst", "flash_pipe_inst", "decode_tc_inst", "decode_pipe_inst",
-                     "decode_stream_inst"):
+                     "decode_stream_inst", "decode_mma_inst"):
             if stem == "decode_tc_inst" and name == "f32":
                 continue  # the tensor-core decode covers block-quantized and f16 K only
-            if stem in ("decode_pipe_inst", "decode_stream_inst") and name in ("f32", "f16"):
+            if stem in ("decode_pipe_inst", "decode_stream_inst", "decode_mma_inst") and name in ("f32", "f16"):
                 continue  # the persistent decodes cover block-quantized K only
             obj = os.path.join(BUILD, f"{stem}_{name}.o")
             units.append((os.path.join(CSRC, f"{stem}.cu"), obj, [f"-DCVATTN_KT={tid}"]))

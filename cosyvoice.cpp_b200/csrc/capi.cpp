@@ -711,7 +711,8 @@ cvattn_status cvattn_kv_cache_attention(cvattn_kv_cache* c, void* stream, int32_
             DeviceGuard dg(c->ctx->device);
             if (dg.error() != cudaSuccess) return from_cuda(dg.error());
             cudaError_t e = launch_fill_lengths(as_stream(stream), c->d_len, c->p.batch, n_kv,
-                                                static_cast<uint32_t*>(c->ws), c->p.batch);
+                                                static_cast<uint32_t*>(c->ws),
+                                                (int)(decode_ticket_bytes(c->p.batch, c->p.n_kv_heads) / 4));
             if (e != cudaSuccess) return from_cuda(e);
         }
         return cvattn_decode(c->ctx, stream, &dp);

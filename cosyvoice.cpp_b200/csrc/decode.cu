@@ -1,6 +1,7 @@
 // decode.cu -- host side of the split-KV decode kernel (decode.cuh) and the
 // standalone log-sum-exp combine used for cross-GPU split-KV partials.
 #include "decode.cuh"
+#include "decode_mma.cuh"
 #include "decode_pipe.cuh"
 #include "decode_stream.cuh"
 #include "decode_tc.cuh"
@@ -36,13 +37,17 @@ bool decode_supported(int k_type, int v_type, int head_dim, int n_q_heads, int n
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+size_t decode_ticket_bytes(int n_seq, int n_kv_heads) {
+    return align256((size_t)n_seq * (size_t)(n_kv_heads > 2 ? n_kv_heads : 2) * 4);
+}
+
 size_t decode_workspace_bytes(int k_type, int v_type, int n_seq, int max_kv_len, int n_q_heads, int n_kv_heads,
                               int head_dim) {
     int C = decode_chunk_positions(k_type, v_type, n_kv_heads, head_dim);
     if (C == 0 || n_seq <= 0 || max_kv_len < 0) return 0;
-    if (C > dstream::kC) C = dstream::kC;  // partial slots for the streaming kernel's 64-position items
+    if (C > dstream::kC) C = dstream::kC;  // partial slots for the 64-position items
     const size_t chunks = (size_t)((max_kv_len + C - 1) / C);
-    return align256((size_t)n_seq * 4) + align256((size_t)n_seq * chunks * n_q_heads * 2 * 4) +
+    return decode_ticket_bytes(n_seq, n_kv_heads) + align256((size_t)n_seq * chunks * n_q_heads * 2 * 4) +
            align256((size_t)n_seq * chunks * n_q_heads * kD * 4);
 }
 
@@ -91,7 +96,7 @@ cudaError_t launch_decode(cudaStream_t stream, const cvattn_decode_params& p, in
         a.rope_attn_factor = rope->attn_factor;
     }
     uint8_t* ws = static_cast<uint8_t*>(p.workspace);
-    const size_t cnt_bytes = align256((size_t)p.n_seq * 4);
+    const size_t cnt_bytes = decode_ticket_bytes(p.n_seq, Hkv);
     const size_t ml_bytes = align256((size_t)p.n_seq * chunks * p.n_q_heads * 2 * 4);
     a.ws_cnt = reinterpret_cast<uint32_t*>(ws);
     a.ws_ml = reinterpret_cast<float*>(ws + cnt_bytes);
@@ -109,6 +114,33 @@ cudaError_t launch_decode(cudaStream_t stream, const cvattn_decode_params& p, in
         // persistent pipelined kernel when its ring of stages fits one SM
         const int num_sms = current_sm_count();
         const bool persistent = !(p.flags & CVATTN_DECODE_NOT_PERSISTENT) && num_sms > 0;
+        // Throughput-bound launches (at least kMmaItemsPerSm 64-position items per SM for the
+        // host bound max_kv_len) run the register-resident warp-MMA kernel: fewer
+        // instructions per item, and every warp pair works on its own range.  Latency-bound
+        // launches run the TMEM streaming kernel, whose per-item pipeline is shorter.
+        // CVATTN_DECODE_WARP_MMA / CVATTN_DECODE_TMEM_STREAM force either; the RoPE-fused
+        // step always runs on the streaming kernel.
+        constexpr long kMmaItemsPerSm = 32;
+        const long items_bound = (long)p.n_seq * ((p.max_kv_len + dmma::kC - 1) / dmma::kC);
+        const bool want_mma = (p.flags & CVATTN_DECODE_WARP_MMA) ||
+                              (!(p.flags & CVATTN_DECODE_TMEM_STREAM) && items_bound >= kMmaItemsPerSm * num_sms);
+        if (persistent && want_mma && !rope && !(p.flags & CVATTN_DECODE_WIDE_CHUNKS) &&
+            dmma::supported_type(p.k.type) && dmma::supported_type(p.v.type) && p.n_seq <= dmma::kMaxSeq) {
+            const int chunks_s = (p.max_kv_len + dmma::kC - 1) / dmma::kC;
+            Args b = a;
+            b.C = dmma::kC;
+            b.ws_chunks = chunks_s;
+            b.ws_ml = reinterpret_cast<float*>(ws + cnt_bytes);
+            b.ws_o = reinterpret_cast<float*>(ws + cnt_bytes + align256((size_t)p.n_seq * chunks_s * p.n_q_heads * 2 * 4));
+            switch (p.k.type) {
+            case kQ4_0: return dmma::launch_for_k<kQ4_0>(stream, b, p.v.type, num_sms);
+            case kQ4_1: return dmma::launch_for_k<kQ4_1>(stream, b, p.v.type, num_sms);
+            case kQ5_0: return dmma::launch_for_k<kQ5_0>(stream, b, p.v.type, num_sms);
+            case kQ5_1: return dmma::launch_for_k<kQ5_1>(stream, b, p.v.type, num_sms);
+            case kQ8_0: return dmma::launch_for_k<kQ8_0>(stream, b, p.v.type, num_sms);
+            default: break;
+            }
+        }
         if (persistent && !(p.flags & CVATTN_DECODE_WIDE_CHUNKS) && dstream::supported_type(p.k.type) &&
             dstream::supported_type(p.v.type) && p.n_seq <= dstream::kMaxSeq &&
             dstream::smem_bytes(p.k.type, p.v.type) <= 227 * 1024) {

@@ -1,0 +1,55 @@
+// decode_mma_inst.cu -- instantiates decode_mma_kernel for one K type
+// (CVATTN_KT) and every block-quantized V type; compiled once per K type.
+#include "decode_mma.cuh"
+
+#ifndef CVATTN_KT
+#error "compile with -DCVATTN_KT=<ggml type id>"
+#endif
+
+namespace cvattn {
+namespace dmma {
+
+// Launch over min(sm_count, ceil(items / pairs)) CTAs of `pairs` warp pairs, with
+// programmatic stream serialization: the kernel waits (griddepcontrol.wait)
+// before it reads an input the previous kernel may still write.
+template <int KT, int VT>
+static cudaError_t run(cudaStream_t s, const Args& a, int n_sms) {
+    auto fn = decode_mma_kernel<KT, VT>;
+    const int rowK = (int)type_row_bytes(KT, 2 * kD), rowV = (int)type_row_bytes(VT, 2 * kD);
+    const long items = (long)a.n_seq * ((a.max_kv_len + kC - 1) / kC);
+    int pairs = max_pairs(KT, VT);
+    const long per_sm = (items + n_sms - 1) / n_sms;
+    if (per_sm < pairs) pairs = (int)(per_sm > 0 ? per_sm : 1);
+
+    const long ctas_needed = (items + pairs - 1) / pairs;
+    const int grid = (int)(ctas_needed < n_sms ? (ctas_needed > 0 ? ctas_needed : 1) : n_sms);
+    const int smem = Smem(rowK, rowV, pairs).total;
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3((unsigned)(64 * pairs));
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, fn, a);
+}
+
+template <>
+cudaError_t launch_for_k<CVATTN_KT>(cudaStream_t s, const Args& a, int vt, int n_sms) {
+    switch (vt) {
+    case kQ4_0: return run<CVATTN_KT, kQ4_0>(s, a, n_sms);
+    case kQ4_1: return run<CVATTN_KT, kQ4_1>(s, a, n_sms);
+    case kQ5_0: return run<CVATTN_KT, kQ5_0>(s, a, n_sms);
+    case kQ5_1: return run<CVATTN_KT, kQ5_1>(s, a, n_sms);
+    case kQ8_0: return run<CVATTN_KT, kQ8_0>(s, a, n_sms);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace dmma
+}  // namespace cvattn

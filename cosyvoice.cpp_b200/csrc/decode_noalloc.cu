@@ -80,7 +80,7 @@ extern "C" cvattn_status cvattn_decode_noalloc(cvattn_context* ctx, void* stream
     int prev = -1;
     if (cudaGetDevice(&prev) != cudaSuccess) return CVATTN_ERR_CUDA;
     if (prev != dev && cudaSetDevice(dev) != cudaSuccess) return CVATTN_ERR_CUDA;
-    const size_t counter_bytes = ((size_t)p->n_seq * 4 + 255) & ~size_t(255);
+    const size_t counter_bytes = cvattn::decode_ticket_bytes(p->n_seq, p->k.n_heads);
     e = cudaMemsetAsync(scratch, 0, counter_bytes, reinterpret_cast<cudaStream_t>(stream));
     if (prev != dev) cudaSetDevice(prev);
     if (e != cudaSuccess) return CVATTN_ERR_CUDA;

@@ -29,6 +29,7 @@
 // key tiles are never loaded.
 #pragma once
 
+#include "decode_tc.cuh"
 #include "flash_tc.cuh"
 
 namespace cvattn {
@@ -59,6 +60,19 @@ constexpr int kKOff = 32 * 1024;                     // kStages x 8 KB
 constexpr int kVOff = kKOff + kStages * kTileBytes;  // kStages x 8 KB
 constexpr int kBarOff = kVOff + kStages * kTileBytes;  // 128 KB
 constexpr int kSmemBytes = kBarOff + 512;            // one CTA per SM (TMEM: 512 columns)
+constexpr int kRawOff = kSmemBytes;                  // staged producer: raw rows of two tiles
+
+__host__ __device__ constexpr bool is_block_quant(int t) {
+    return t == kQ4_0 || t == kQ4_1 || t == kQ5_0 || t == kQ5_1 || t == kQ8_0;
+}
+// Bytes of the raw K and V head rows of one 64-key tile (staged producer).
+__host__ __device__ constexpr int raw_tile_bytes(int kt, int vt) {
+    return (kBN * 2 * (group_bytes(kt) + group_bytes(vt)) + 127) / 128 * 128;
+}
+// Dynamic shared memory of flash_pipe_kernel<KT, VT>.
+__host__ __device__ constexpr int smem_bytes(int kt, int vt) {
+    return (is_block_quant(kt) && is_block_quant(vt)) ? kRawOff + 2 * raw_tile_bytes(kt, vt) : kSmemBytes;
+}
 
 struct Bars {
     uint64_t kv_full[kStages];
@@ -235,6 +249,145 @@ __device__ __forceinline__ void exp_pass(uint32_t s_taddr, uint32_t p_taddr, boo
     }
     pm = fmaxf(__low2float(pmax), __high2float(pmax));
     lt = (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y);
+}
+
+
+// ------------------------------------------------- staged producer (quantized K/V)
+//
+// The 128 producer threads copy a tile's raw K and V head rows into shared
+// memory with coalesced 4-byte cp.async (one tile ahead, two raw buffers), then
+// convert them there: thread r takes row r & 63 and block r >> 6 of K, then of
+// V (the block is uniform per warp), builds the block's 32 quants as exact f16
+// integers (centred for the 4/5-bit types) and scales them in f16 with one
+// rounding (hmul2, or hfma2 with the centred min), i.e. the same f16 value the
+// dequantize-then-round path gives for the _0 types.
+
+__device__ __forceinline__ void prod_bar(int id, int n) { asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(n) : "memory"); }
+
+__device__ __forceinline__ bool prod_bar_and(int id, int n, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r) : "r"((uint32_t)v), "r"(id), "r"(n) : "memory");
+    return r != 0;
+}
+
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"(smem_addr(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+
+// Block `blk` of raw head row g (2-byte aligned in shared memory) -> f16 chunks
+// blk * 4 .. blk * 4 + 3 of row `row` of a 128B-swizzled tile; zeros past n_kv.
+template <int T>
+__device__ __forceinline__ void convert_block_f16(const uint8_t* g, bool valid, uint8_t* tile, int row, int blk) {
+    uint32_t w[16];
+    if (valid) {
+        float d, m;
+        dtc::convert_group<T>(g, w, d, m);
+        const __half2 d2 = __float2half2_rn(d);
+        if constexpr (BlockTraits<T>::HAS_MIN) {
+            const __half2 m2 = __float2half2_rn(m);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const __half2 x = __hfma2(*reinterpret_cast<const __half2*>(&w[i]), d2, m2);
+                w[i] = *reinterpret_cast<const uint32_t*>(&x);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const __half2 x = __hmul2(*reinterpret_cast<const __half2*>(&w[i]), d2);
+                w[i] = *reinterpret_cast<const uint32_t*>(&x);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[i] = 0u;
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(tile + tc::sw128_offset(row, blk * 4 + c)) =
+            make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+}
+
+// The producer role for block-quantized K and V (128 threads, r = 0..127).
+// Tiles are produced in the order the MMA issuers consume them.
+template <int KT, int VT>
+__device__ __forceinline__ void produce_staged(const Params& p, uint8_t* smem, Bars* B, int total, int r) {
+    constexpr int HBK = 2 * group_bytes(KT), HBV = 2 * group_bytes(VT);  // bytes of one head row
+    constexpr int WK = HBK / 4, WV = HBV / 4;
+    constexpr int RB = raw_tile_bytes(KT, VT);
+    constexpr int kBar = 1;  // named barrier of the 128 producer threads
+    uint8_t* raw0 = smem + kRawOff;
+    // first tile at or after (item idx, tile j)
+    auto seek = [&](int& idx, int& j, int& b, int& g) -> bool {
+        while (idx < total) {
+            const Item it = item_at(p, idx);
+            const int n = max(tiles_of(p, it.active[0], it.qt[0]), tiles_of(p, it.active[1], it.qt[1]));
+            if (j < n) {
+                b = it.b;
+                g = it.g;
+                return true;
+            }
+            idx += gridDim.x;
+            j = 0;
+        }
+        return false;
+    };
+    auto issue = [&](int b, int g, int j, uint8_t* dst) {
+        const uint8_t* kb = p.k + (int64_t)b * p.k_nb2 + (int64_t)g * HBK;
+        const uint8_t* vb = p.v + (int64_t)b * p.v_nb2 + (int64_t)g * HBV;
+        for (int w = r; w < kBN * WK; w += 128) {
+            const int row = w / WK, wi = w - row * WK;
+            const int key = j * kBN + row;
+            if (key < p.n_kv) cp_async4(dst + row * HBK + 4 * wi, kb + (int64_t)key * p.k_nb1 + 4 * wi);
+        }
+        uint8_t* vdst = dst + kBN * HBK;
+        for (int w = r; w < kBN * WV; w += 128) {
+            const int row = w / WV, wi = w - row * WV;
+            const int key = j * kBN + row;
+            if (key < p.n_kv) cp_async4(vdst + row * HBV + 4 * wi, vb + (int64_t)key * p.v_nb1 + 4 * wi);
+        }
+        cp_async_commit();
+    };
+    int idx = blockIdx.x, jt = 0, b = 0, g = 0;
+    bool have = seek(idx, jt, b, g);
+    if (have) issue(b, g, jt, raw0);
+    const int row = r & (kBN - 1), blk = r >> 6;
+    for (uint32_t n = 0; have; ++n) {
+        int idx2 = idx, jt2 = jt + 1, b2 = 0, g2 = 0;
+        const bool have2 = seek(idx2, jt2, b2, g2);
+        prod_bar(kBar, 128);  // tile n - 1 is converted: its raw buffer takes tile n + 1
+        if (have2) {
+            issue(b2, g2, jt2, raw0 + ((n + 1) & 1) * RB);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        const int s = n % kStages;
+        const uint32_t use = n / kStages;
+        const bool ok = use == 0 || wait_or_err(&B->kv_empty[s], (use - 1) & 1, &B->err, p.status, 5);
+        // every thread's copies of tile n have landed and stage s is free (or all stop together)
+        if (!prod_bar_and(kBar, 128, ok)) break;
+        const uint8_t* raw = raw0 + (n & 1) * RB;
+        const bool valid = jt * kBN + row < p.n_kv;
+        convert_block_f16<KT>(raw + row * HBK + blk * group_bytes(KT), valid, smem + kKOff + s * kTileBytes, row, blk);
+        convert_block_f16<VT>(raw + kBN * HBK + row * HBV + blk * group_bytes(VT), valid, smem + kVOff + s * kTileBytes,
+                              row, blk);
+        fence_proxy_async_smem();
+        mbar_arrive(&B->kv_full[s]);
+        idx = idx2;
+        jt = jt2;
+        b = b2;
+        g = g2;
+        have = have2;
+    }
+    cp_async_wait<0>();  // no copy into shared memory outlives the CTA
 }
 
 template <int KT, int VT>
@@ -428,6 +581,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp < kMmaWarp) {
         // ====================================================== producer
         const int r = tid - kProdWarp0 * 32;  // 0..127 = key row of the tile
+        if constexpr (is_block_quant(KT) && is_block_quant(VT)) {
+            if (p.staged) {
+                produce_staged<KT, VT>(p, smem, B, total, r);
+                goto producer_done;
+            }
+        }
+        {
         uint32_t n_kv_tiles = 0;
         for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
             const Item it = item_at(p, idx);
@@ -467,6 +627,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (!ok || *reinterpret_cast<volatile int*>(&B->err)) break;
         }
+        }
+    producer_done:;
     } else if (warp >= kMmaWarp && lane == 0) {
         // ====================================================== MMA issuer of query tile x
         const int x = warp - kMmaWarp;

@@ -12,9 +12,10 @@ namespace fp {
 template <int KT, int VT>
 static cudaError_t run(cudaStream_t s, const Params& p, const CUtensorMap& km, const CUtensorMap& vm, dim3 grid) {
     auto fn = flash_pipe_kernel<KT, VT>;
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    constexpr int smem = smem_bytes(KT, VT);
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    fn<<<grid, kThreads, kSmemBytes, s>>>(p, km, vm);
+    fn<<<grid, kThreads, smem, s>>>(p, km, vm);
     return cudaGetLastError();
 }
 

@@ -106,6 +106,11 @@ cudaError_t launch_flash(cudaStream_t stream, const cvattn_flash_params& a, int*
             ((reinterpret_cast<uintptr_t>(a.v.data) & 15) || (a.v.nb1 & 15) || (a.v.nb2 & 15)))
             return cudaErrorInvalidValue;
     }
+    // block-quantized K and V with 4-byte aligned rows go through the staged producer
+    // (coalesced cp.async of the raw rows, conversion in shared memory)
+    p.staged = fp::is_block_quant(a.k.type) && fp::is_block_quant(a.v.type) &&
+               ((reinterpret_cast<uintptr_t>(a.k.data) | reinterpret_cast<uintptr_t>(a.v.data)) & 3) == 0 &&
+               ((a.k.nb1 | a.k.nb2 | a.v.nb1 | a.v.nb2) & 3) == 0;
     if (!(a.flags & CVATTN_FLASH_ONE_TILE)) {
         // persistent kernel: one CTA per SM over the query-tile pairs
         const int num_sms = current_sm_count();

@@ -35,6 +35,9 @@ cudaError_t launch_fill_lengths(cudaStream_t stream, int32_t* lens, int n, int32
 
 // decode.cu
 int decode_chunk_positions(int k_type, int v_type, int n_kv_heads, int head_dim);
+// Bytes of the ticket block that leads a decode workspace: one 32-bit counter
+// per (sequence, KV head), 256-byte aligned.
+size_t decode_ticket_bytes(int n_seq, int n_kv_heads);
 size_t decode_workspace_bytes(int k_type, int v_type, int n_seq, int max_kv_len, int n_q_heads, int n_kv_heads, int head_dim);
 bool decode_supported(int k_type, int v_type, int head_dim, int n_q_heads, int n_kv_heads);
 cudaError_t launch_decode(cudaStream_t stream, const cvattn_decode_params& p, int* status,

@@ -31,6 +31,8 @@ DECODE_CUDA_CORES = 2
 DECODE_NOT_PERSISTENT = 4
 DECODE_INPUTS_READY = 8
 DECODE_WIDE_CHUNKS = 16
+DECODE_TMEM_STREAM = 32
+DECODE_WARP_MMA = 64
 FLASH_ONE_TILE = 1
 ROPE_NORMAL, ROPE_NEOX = 0, 2
 
@@ -216,7 +218,8 @@ class Decoder:
                  q, out, kv_len, k_new=None, v_new=None, k_seq_ptrs=None, v_seq_ptrs=None,
                  scale: float | None = None, emit_partial: bool = False, partial_ml=None, workspace=None,
                  cuda_cores: bool = False, not_persistent: bool = False, inputs_ready: bool = False,
-                 wide_chunks: bool = False, rope: RopeParams | None = None):
+                 wide_chunks: bool = False, tmem_stream: bool = False, warp_mma: bool = False,
+                 rope: RopeParams | None = None):
         self.ctx = ctx
         self.rope = rope
         p = DecodeParams()
@@ -230,7 +233,8 @@ class Decoder:
         p.n_seq, p.n_q_heads, p.max_kv_len = n_seq, n_q_heads, max_kv_len
         p.flags = ((DECODE_EMIT_PARTIAL if emit_partial else 0) | (DECODE_CUDA_CORES if cuda_cores else 0)
                    | (DECODE_NOT_PERSISTENT if not_persistent else 0) | (DECODE_INPUTS_READY if inputs_ready else 0)
-                   | (DECODE_WIDE_CHUNKS if wide_chunks else 0))
+                   | (DECODE_WIDE_CHUNKS if wide_chunks else 0) | (DECODE_TMEM_STREAM if tmem_stream else 0)
+                   | (DECODE_WARP_MMA if warp_mma else 0))
         p.scale = 1.0 / math.sqrt(k.head_dim) if scale is None else scale
         need = decode_workspace_size(k.type, v.type, n_seq, max_kv_len, n_q_heads, k.n_heads, k.head_dim)
         if workspace is None:

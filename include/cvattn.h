@@ -204,7 +204,17 @@ enum {
     CVATTN_DECODE_INPUTS_READY = 8,
     /* use the persistent kernel with 128-position items and a per-chunk merge
      * instead of the default streaming one (64-position items, running output) */
-    CVATTN_DECODE_WIDE_CHUNKS = 16
+    CVATTN_DECODE_WIDE_CHUNKS = 16,
+    /* Block-quantized K and V (2 KV heads, head_dim 64) have two persistent
+     * tensor-core kernels: the tcgen05 streaming kernel (tiles in shared memory,
+     * running output in tensor memory; shorter per-item pipeline) and the
+     * register-resident warp-MMA kernel (fewer instructions per item).  By
+     * default a launch with at least 32 64-position items per SM (counted from
+     * n_seq and max_kv_len) runs the warp-MMA kernel, smaller ones the streaming
+     * kernel; these flags force one.  cvattn_decode_rope always runs on the
+     * streaming kernel. */
+    CVATTN_DECODE_TMEM_STREAM = 32,
+    CVATTN_DECODE_WARP_MMA = 64
 };
 
 /* One decode token per sequence: ggml_flash_attn_ext with n_q = 1 and no mask

@@ -55,7 +55,7 @@ def reference(oracle, kt, vt, kq, vq, q, lens):
     return out
 
 
-PATHS = {"streaming": {}, "wide": {"wide_chunks": True}, "tensor_cores": {"not_persistent": True},
+PATHS = {"warp_mma": {"warp_mma": True}, "tmem_stream": {"tmem_stream": True}, "wide": {"wide_chunks": True}, "tensor_cores": {"not_persistent": True},
          "cuda_cores": {"cuda_cores": True}}
 
 
@@ -122,7 +122,8 @@ def test_decode_fused_append(ctx, cv, cuda, oracle, kname, vname, path):
     assert rel_l2(out, ref) <= REL_L2
 
 
-def test_decode_separate_worker_buffers(ctx, cv, cuda, oracle):
+@pytest.mark.parametrize("path", ["warp_mma", "tmem_stream"])
+def test_decode_separate_worker_buffers(ctx, cv, cuda, oracle, path):
     """Per-sequence row pointers: each worker owns its own cache buffer."""
     torch = cuda
     kt = vt = cv.Q8_0
@@ -143,7 +144,7 @@ def test_decode_separate_worker_buffers(ctx, cv, cuda, oracle):
     q = rng.standard_normal((len(lens), HQ, D)).astype(np.float32)
     kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
     out = cv.decode(ctx, torch.tensor(q, device="cuda"), desc_k, desc_v, kl, max(lens),
-                    k_seq_ptrs=kp, v_seq_ptrs=vp).cpu().numpy()
+                    k_seq_ptrs=kp, v_seq_ptrs=vp, **PATHS[path]).cpu().numpy()
     for s, L in enumerate(lens):
         kd = oracle.dequantize(kt, kqs[s], HKV * D).reshape(L, HKV, D)
         vd = oracle.dequantize(vt, vqs[s], HKV * D).reshape(L, HKV, D)
@@ -151,7 +152,8 @@ def test_decode_separate_worker_buffers(ctx, cv, cuda, oracle):
         assert rel_l2(out[s], ref) <= REL_L2
 
 
-def test_decode_split_partials_and_combine(ctx, cv, cuda, oracle):
+@pytest.mark.parametrize("path", ["warp_mma", "tmem_stream"])
+def test_decode_split_partials_and_combine(ctx, cv, cuda, oracle, path):
     """Long-context split-KV: two position shards emit partials, combine merges them."""
     torch = cuda
     kt, vt = cv.Q8_0, cv.Q4_0
@@ -169,13 +171,14 @@ def test_decode_split_partials_and_combine(ctx, cv, cuda, oracle):
         vp = torch.tensor([vb.data_ptr() + start * rbv], dtype=torch.int64, device="cuda")
         kl = torch.tensor([n], dtype=torch.int32, device="cuda")
         cv.decode(ctx, qt, kd, vd, kl, n, out=po[part:part + 1], k_seq_ptrs=kp, v_seq_ptrs=vp,
-                  emit_partial=True, partial_ml=pml[part:part + 1])
+                  emit_partial=True, partial_ml=pml[part:part + 1], **PATHS[path])
     out = cv.combine(po, pml).cpu().numpy().reshape(1, HQ, D)
     ref = reference(oracle, kt, vt, kq, vq, q, [L])
     assert rel_l2(out, ref) <= REL_L2
 
 
-def test_decode_zero_and_invalid_lengths(ctx, cv, cuda, oracle):
+@pytest.mark.parametrize("path", ["warp_mma", "tmem_stream"])
+def test_decode_zero_and_invalid_lengths(ctx, cv, cuda, oracle, path):
     torch = cuda
     kt = vt = cv.Q8_0
     rng = np.random.default_rng(13)
@@ -183,14 +186,15 @@ def test_decode_zero_and_invalid_lengths(ctx, cv, cuda, oracle):
     q = torch.tensor(rng.standard_normal((3, HQ, D)).astype(np.float32), device="cuda")
     # seq 0 empty -> zeros; seq 2 longer than the launch bound -> zeros + status
     kl = torch.tensor([0, 150, 190], dtype=torch.int32, device="cuda")
-    out = cv.decode(ctx, q, kd, vd, kl, 160).cpu().numpy()
+    out = cv.decode(ctx, q, kd, vd, kl, 160, **PATHS[path]).cpu().numpy()
     assert not out[0].any() and not out[2].any()
     assert np.abs(out[1]).sum() > 0
     st, detail = ctx.sync_status()
     assert st == 6 and detail == 2
 
 
-def test_decode_workspace_reuse_many_calls(ctx, cv, cuda, oracle):
+@pytest.mark.parametrize("path", ["warp_mma", "tmem_stream"])
+def test_decode_workspace_reuse_many_calls(ctx, cv, cuda, oracle, path):
     """The ticket counters return to zero: repeated calls on one workspace agree."""
     torch = cuda
     kt = vt = cv.Q8_0
@@ -200,7 +204,7 @@ def test_decode_workspace_reuse_many_calls(ctx, cv, cuda, oracle):
     q = torch.tensor(rng.standard_normal((4, HQ, D)).astype(np.float32), device="cuda")
     kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
     out = torch.empty_like(q)
-    dec = cv.Decoder(ctx, kd, vd, 4, HQ, 2048, q, out, kl)
+    dec = cv.Decoder(ctx, kd, vd, 4, HQ, 2048, q, out, kl, **PATHS[path])
     dec()
     first = out.clone()
     for _ in range(20):
@@ -209,8 +213,9 @@ def test_decode_workspace_reuse_many_calls(ctx, cv, cuda, oracle):
     assert torch.equal(first, out)
 
 
+@pytest.mark.parametrize("path", ["warp_mma", "tmem_stream"])
 @pytest.mark.parametrize("qscale,vscale", [(1e-3, 1.0), (300.0, 1.0), (1.0, 1e3), (1.0, 1e-4)])
-def test_decode_tensor_core_scaling_extremes(ctx, cv, cuda, oracle, qscale, vscale):
+def test_decode_tensor_core_scaling_extremes(ctx, cv, cuda, oracle, qscale, vscale, path):
     """Q and V magnitudes far from 1 keep the f32 bar (exact power-of-two scaling of the hi/lo splits)."""
     torch = cuda
     kt, vt = cv.Q8_0, cv.Q5_1
@@ -224,12 +229,12 @@ def test_decode_tensor_core_scaling_extremes(ctx, cv, cuda, oracle, qscale, vsca
     vd = cv.kv_tensor(torch.tensor(vq.reshape(-1), device="cuda"), vt, HKV, D, cap, 2)
     q = (rng.standard_normal((2, HQ, D)) * qscale).astype(np.float32)
     kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
-    out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, cap).cpu().numpy()
+    out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, cap, **PATHS[path]).cpu().numpy()
     ref = reference(oracle, kt, vt, kq, vq, q, lens)
     assert rel_l2(out, ref) <= REL_L2, f"rel-L2 {rel_l2(out, ref):.3e}"
 
 
-@pytest.mark.parametrize("path", ["streaming", "wide", "tensor_cores"])
+@pytest.mark.parametrize("path", ["warp_mma", "tmem_stream", "wide", "tensor_cores"])
 @pytest.mark.parametrize("kname,vname", [("q8_0", "q4_0"), ("q5_1", "q5_1")])
 def test_decode_many_chunks_per_sm(ctx, cv, cuda, oracle, kname, vname, path):
     """Hundreds of sequences: each persistent CTA walks a range of several
@@ -250,7 +255,8 @@ def test_decode_many_chunks_per_sm(ctx, cv, cuda, oracle, kname, vname, path):
     assert np.abs(out - ref).max() <= MAX_ABS
 
 
-def test_decode_many_chunks_emit_partial(ctx, cv, cuda, oracle):
+@pytest.mark.parametrize("path", ["warp_mma", "tmem_stream"])
+def test_decode_many_chunks_emit_partial(ctx, cv, cuda, oracle, path):
     """Partials (unnormalized O, max in log2 units, sum) of the merged runs."""
     torch = cuda
     kt = vt = cv.Q8_0
@@ -261,7 +267,7 @@ def test_decode_many_chunks_emit_partial(ctx, cv, cuda, oracle):
     kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
     pml = torch.zeros((len(lens), HQ, 2), dtype=torch.float32, device="cuda")
     out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, 2048, emit_partial=True,
-                    partial_ml=pml).cpu().numpy()
+                    partial_ml=pml, **PATHS[path]).cpu().numpy()
     ml = pml.cpu().numpy()
     ref = reference(oracle, kt, vt, kq, vq, q, lens)
     assert rel_l2(out / ml[:, :, 1:2], ref) <= REL_L2
@@ -273,7 +279,8 @@ def test_decode_many_chunks_emit_partial(ctx, cv, cuda, oracle):
             assert abs(ml[s, h, 0] - smax) <= 1e-4 * max(1.0, abs(smax))
 
 
-def test_decode_long_sequences_direct_combine(ctx, cv, cuda, oracle):
+@pytest.mark.parametrize("path", ["warp_mma", "tmem_stream"])
+def test_decode_long_sequences_direct_combine(ctx, cv, cuda, oracle, path):
     """More than 64 chunks per sequence: the merge streams every chunk slot and skips empty ones."""
     torch = cuda
     kt, vt = cv.Q8_0, cv.Q8_0
@@ -282,12 +289,13 @@ def test_decode_long_sequences_direct_combine(ctx, cv, cuda, oracle):
     kq, vq, kb, vb, kd, vd = build(cv, cuda, oracle, kt, vt, lens, rng, cap=9000)
     q = rng.standard_normal((len(lens), HQ, D)).astype(np.float32)
     kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
-    out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, 9000).cpu().numpy()
+    out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, 9000, **PATHS[path]).cpu().numpy()
     ref = reference(oracle, kt, vt, kq, vq, q, lens)
     assert rel_l2(out, ref) <= REL_L2, f"rel-L2 {rel_l2(out, ref):.3e}"
 
 
-def test_decode_step_of_layers_inputs_ready(ctx, cv, cuda, oracle):
+@pytest.mark.parametrize("path", ["warp_mma", "tmem_stream"])
+def test_decode_step_of_layers_inputs_ready(ctx, cv, cuda, oracle, path):
     """One model step of several layers launched back to back with the fused
     append and DECODE_INPUTS_READY (each launch streams its K/V while the
     previous layer finishes), repeated for two steps: outputs and appended rows
@@ -306,7 +314,7 @@ def test_decode_step_of_layers_inputs_ready(ctx, cv, cuda, oracle):
         qt, kt_, vt_ = (torch.tensor(x, device="cuda") for x in (q, knew, vnew))
         outs = torch.empty_like(qt)
         decs = [cv.Decoder(ctx, caches[l][4], caches[l][5], n, HQ, cap, qt[l], outs[l], kl, k_new=kt_[l], v_new=vt_[l],
-                           inputs_ready=True) for l in range(layers)]
+                           inputs_ready=True, **PATHS[path]) for l in range(layers)]
         for d in decs:
             d()
         got = outs.cpu().numpy()
@@ -323,7 +331,7 @@ def test_decode_step_of_layers_inputs_ready(ctx, cv, cuda, oracle):
         assert np.array_equal(caches[l][2].view(n, cap, -1).cpu().numpy(), caches[l][0]), "appended K rows"
 
 
-@pytest.mark.parametrize("path", ["streaming", "wide"])
+@pytest.mark.parametrize("path", ["warp_mma", "tmem_stream", "wide"])
 @pytest.mark.parametrize("kname,vname", [("q8_0", "q8_0"), ("q4_1", "q5_1")])
 def test_decode_running_rescales(ctx, cv, cuda, oracle, kname, vname, path):
     """Scores that grow along the sequence and V magnitudes that jump by 2^+-9

@@ -37,7 +37,7 @@ def with_outliers(rng, shape):
     return x
 
 
-PATHS = {"streaming": {}, "wide": {"wide_chunks": True}, "tensor_cores": {"not_persistent": True},
+PATHS = {"warp_mma": {"warp_mma": True}, "tmem_stream": {"tmem_stream": True}, "wide": {"wide_chunks": True}, "tensor_cores": {"not_persistent": True},
          "cuda_cores": {"cuda_cores": True}}
 
 
