@@ -551,12 +551,15 @@ def run_decode_cfg4_sharded(torch, cv, ctx, rank: int, world: int, dist, reps: i
         gbs = nbytes_total / (ms * 1e-3) / 1e9
         achieved = nbytes_rank / (ms_rank * 1e-3) / 1e9
         key = "decode_cfg4_" + name.replace("/", "_")
+        # the dispatcher's rule (csrc/decode.cu): at least 32 64-position items per SM -> warp-MMA kernel
+        n_sms = torch.cuda.get_device_properties(0).multi_processor_count
+        kname = "decode_mma_kernel" if mine * (L // 64) >= 32 * n_sms else "decode_stream_kernel"
         res[key] = {
             "what": f"decode 256 seqs x 4096, {name}, one layer, sequences sharded over {world} GPU(s)",
             "gbs": round(gbs, 1), "us_per_launch": round(ms * 1000.0, 2), "seqs_per_gpu": mine,
             "bytes_per_launch": nbytes_total, "frac_hbm_peak": round(gbs / world / peaks["hbm_gbs"], 4),
             "scaling": "strong",
-            "roofline": {"bound": "hbm", "kernel": f"decode_stream_kernel<{name.replace('/', ',')}>",
+            "roofline": {"bound": "hbm", "kernel": f"{kname}<{name.replace('/', ',')}>",
                          "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
                          "algorithmic_bytes_per_launch": nbytes_rank,
@@ -820,6 +823,69 @@ def cpu_baseline_for_line(budget_s: float = 10.0) -> dict:
             "sample": f"{len(times)} samples of {SAMPLE_DESC}"}
 
 
+def run_cpu_baselines(budget_s: float = 4.0) -> dict:
+    """The oracle's ggml-CPU-style flash attention (the reference's CPU path restated;
+    ggml itself is unavailable) on bounded samples of every config, all host threads.
+    Prints reported baselines; nothing here is a GPU figure."""
+    from oracle import oracle as O
+    O.build()
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(3)
+
+    def timed(fn) -> float:
+        fn()
+        times, t_end = [], time.perf_counter() + budget_s
+        while time.perf_counter() < t_end or len(times) < 2:
+            t0 = time.perf_counter()
+            fn()
+            times.append(time.perf_counter() - t0)
+        return statistics.median(times)
+
+    res = {"kind": "port", "cores": threads, "impl": "oracle/cvattn_oracle.c oracle_flash_cpu (ggml-CPU-style, f32)"}
+    # configs[0]: batch 1, L 512, f16 K/V ~ N(0, 0.5)
+    L = 512
+    k0 = O.quantize(O.F16, 0.5 * rng.standard_normal((L, HKV * D)).astype(np.float32))
+    v0 = O.quantize(O.F16, 0.5 * rng.standard_normal((L, HKV * D)).astype(np.float32))
+    q0 = rng.standard_normal((1, 1, HQ, D)).astype(np.float32)
+    t = timed(lambda: O.flash_cpu(q0, [k0], [v0], O.F16, O.F16, HKV, np.array([L], np.int32), False, 0.125, threads))
+    res["configs0"] = {"us_per_layer": round(t * 1e6, 1), "gbs": round(L * 2 * 256 / t / 1e9, 3)}
+    # configs[1]: the 64-sequence mix, one layer
+    run, sample_bytes, _ = _reference_sample()
+    t = timed(run)
+    res["configs1_mix"] = {"ms_per_layer": round(t * 1e3, 2), "gbs": round(sample_bytes / t / 1e9, 3)}
+    # configs[2]: causal prefill, batch 8, f16 cache, one layer (S = 256 and 1024)
+    for S in (256, 1024):
+        kk = [O.quantize(O.F16, rng.standard_normal((S, HKV * D)).astype(np.float32)) for _ in range(8)]
+        vv = [O.quantize(O.F16, rng.standard_normal((S, HKV * D)).astype(np.float32)) for _ in range(8)]
+        qq = rng.standard_normal((8, S, HQ, D)).astype(np.float32)
+        t = timed(lambda: O.flash_cpu(qq, kk, vv, O.F16, O.F16, HKV, np.full(8, S, np.int32), True, 0.125, threads))
+        res[f"configs2_S{S}"] = {"ms_per_layer": round(t * 1e3, 2),
+                                 "tflops": round(4.0 * D * HQ * 8 * S * (S + 1) / 2 / t / 1e12, 4)}
+    # configs[3]: 16 of the 256 sequences x 4096, q8_0 / q4_0 with 1% +-8 sigma outliers
+    n3, L3 = 16, 4096
+    def outl(shape):
+        x = rng.standard_normal(shape).astype(np.float32)
+        hit = rng.random(shape) < 0.01
+        x[hit] = np.where(rng.random(int(hit.sum())) < 0.5, -8.0, 8.0)
+        return x
+    kk = [O.quantize(O.Q8_0, outl((L3, HKV * D))) for _ in range(n3)]
+    vv = [O.quantize(O.Q4_0, outl((L3, HKV * D))) for _ in range(n3)]
+    qq = rng.standard_normal((n3, 1, HQ, D)).astype(np.float32)
+    t = timed(lambda: O.flash_cpu(qq, kk, vv, O.Q8_0, O.Q4_0, HKV, np.full(n3, L3, np.int32), False, 0.125, threads))
+    res["configs3_q8_0_q4_0"] = {"sample": "16 of 256 sequences, one layer", "ms": round(t * 1e3, 2),
+                                 "gbs": round(n3 * L3 * (136 + 72) / t / 1e9, 3)}
+    # configs[4]: one utterance (CFG batch 2), 16 heads, 600 queries over 900 keys, q8_0 / q4_0, one layer
+    # (the CPU restatement has no chunk mask: it runs every pair, and the rate counts every pair)
+    H, S4, K4 = 16, 600, 900
+    kk = [O.quantize(O.Q8_0, rng.standard_normal((K4, H * D)).astype(np.float32)) for _ in range(2)]
+    vv = [O.quantize(O.Q4_0, rng.standard_normal((K4, H * D)).astype(np.float32)) for _ in range(2)]
+    qq = rng.standard_normal((2, S4, H, D)).astype(np.float32)
+    t = timed(lambda: O.flash_cpu(qq, kk, vv, O.Q8_0, O.Q4_0, H, np.full(2, K4, np.int32), False, 0.125, threads))
+    res["configs4_one_utterance_layer"] = {"ms": round(t * 1e3, 2),
+                                           "tflops": round(4.0 * D * H * 2 * S4 * K4 / t / 1e12, 4)}
+    return res
+
+
 def run_profile(args, torch) -> None:
     """Launch one kernel of the benchmark workload args.steps times, untimed."""
     import cvattn as cv
@@ -852,6 +918,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-secondary", action="store_true", help="headline only: skip every secondary line")
+    ap.add_argument("--cpu-baselines", action="store_true",
+                    help="time the oracle's CPU restatement on bounded samples of every config and print them")
     ap.add_argument("--profile", choices=["decode", "decode_cfg4", "decode_cfg4_q5_1", "dit", "dit_q8_0_q4_0",
                                           "prefill"], default=None,
                     help="only launch the named kernel a few times (for an ncu capture); prints nothing")
@@ -861,6 +929,10 @@ def main() -> None:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
 
+    if args.cpu_baselines:
+        if rank == 0:
+            print(json.dumps(run_cpu_baselines()), flush=True)
+        return
     if args.impl == "reference":
         if rank == 0:
             print(json.dumps(run_reference(args)), flush=True)
