@@ -324,47 +324,57 @@ __device__ __forceinline__ void produce_staged(const Params& p, uint8_t* smem, B
     constexpr int RB = raw_tile_bytes(KT, VT);
     constexpr int kBar = 1;  // named barrier of the 128 producer threads
     uint8_t* raw0 = smem + kRawOff;
-    // first tile at or after (item idx, tile j)
-    auto seek = [&](int& idx, int& j, int& b, int& g) -> bool {
-        while (idx < total) {
-            const Item it = item_at(p, idx);
-            const int n = max(tiles_of(p, it.active[0], it.qt[0]), tiles_of(p, it.active[1], it.qt[1]));
-            if (j < n) {
-                b = it.b;
-                g = it.g;
+    // tile cursor: item idx (its batch entry, KV head and key-tile count) and tile j;
+    // item_at / tiles_of run once per item, not once per tile
+    struct Cursor {
+        int idx, j, nt, b, g;
+    };
+    auto find_item = [&](Cursor& c) -> bool {  // the first item at or after c.idx with a key tile
+        while (c.idx < total) {
+            const Item it = item_at(p, c.idx);
+            c.nt = max(tiles_of(p, it.active[0], it.qt[0]), tiles_of(p, it.active[1], it.qt[1]));
+            if (c.nt > 0) {
+                c.b = it.b;
+                c.g = it.g;
+                c.j = 0;
                 return true;
             }
-            idx += gridDim.x;
-            j = 0;
+            c.idx += gridDim.x;
         }
         return false;
     };
-    auto issue = [&](int b, int g, int j, uint8_t* dst) {
-        const uint8_t* kb = p.k + (int64_t)b * p.k_nb2 + (int64_t)g * HBK;
-        const uint8_t* vb = p.v + (int64_t)b * p.v_nb2 + (int64_t)g * HBV;
+    auto advance = [&](Cursor& c) -> bool {
+        if (++c.j < c.nt) return true;
+        c.idx += gridDim.x;
+        return find_item(c);
+    };
+    auto issue = [&](const Cursor& c, uint8_t* dst) {
+        const uint8_t* kb = p.k + (int64_t)c.b * p.k_nb2 + (int64_t)c.g * HBK + (int64_t)c.j * kBN * p.k_nb1;
+        const uint8_t* vb = p.v + (int64_t)c.b * p.v_nb2 + (int64_t)c.g * HBV + (int64_t)c.j * kBN * p.v_nb1;
+        const int rows = min(kBN, p.n_kv - c.j * kBN);
+#pragma unroll 4
         for (int w = r; w < kBN * WK; w += 128) {
             const int row = w / WK, wi = w - row * WK;
-            const int key = j * kBN + row;
-            if (key < p.n_kv) cp_async4(dst + row * HBK + 4 * wi, kb + (int64_t)key * p.k_nb1 + 4 * wi);
+            if (row < rows) cp_async4(dst + row * HBK + 4 * wi, kb + (int64_t)row * p.k_nb1 + 4 * wi);
         }
         uint8_t* vdst = dst + kBN * HBK;
+#pragma unroll 4
         for (int w = r; w < kBN * WV; w += 128) {
             const int row = w / WV, wi = w - row * WV;
-            const int key = j * kBN + row;
-            if (key < p.n_kv) cp_async4(vdst + row * HBV + 4 * wi, vb + (int64_t)key * p.v_nb1 + 4 * wi);
+            if (row < rows) cp_async4(vdst + row * HBV + 4 * wi, vb + (int64_t)row * p.v_nb1 + 4 * wi);
         }
         cp_async_commit();
     };
-    int idx = blockIdx.x, jt = 0, b = 0, g = 0;
-    bool have = seek(idx, jt, b, g);
-    if (have) issue(b, g, jt, raw0);
+    Cursor cur{(int)blockIdx.x, 0, 0, 0, 0};
+    bool have = find_item(cur);
+    if (have) issue(cur, raw0);
     const int row = r & (kBN - 1), blk = r >> 6;
     for (uint32_t n = 0; have; ++n) {
-        int idx2 = idx, jt2 = jt + 1, b2 = 0, g2 = 0;
-        const bool have2 = seek(idx2, jt2, b2, g2);
+        Cursor nxt = cur;
+        const bool have2 = advance(nxt);
         prod_bar(kBar, 128);  // tile n - 1 is converted: its raw buffer takes tile n + 1
         if (have2) {
-            issue(b2, g2, jt2, raw0 + ((n + 1) & 1) * RB);
+            issue(nxt, raw0 + ((n + 1) & 1) * RB);
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
@@ -375,16 +385,13 @@ __device__ __forceinline__ void produce_staged(const Params& p, uint8_t* smem, B
         // every thread's copies of tile n have landed and stage s is free (or all stop together)
         if (!prod_bar_and(kBar, 128, ok)) break;
         const uint8_t* raw = raw0 + (n & 1) * RB;
-        const bool valid = jt * kBN + row < p.n_kv;
+        const bool valid = cur.j * kBN + row < p.n_kv;
         convert_block_f16<KT>(raw + row * HBK + blk * group_bytes(KT), valid, smem + kKOff + s * kTileBytes, row, blk);
         convert_block_f16<VT>(raw + kBN * HBK + row * HBV + blk * group_bytes(VT), valid, smem + kVOff + s * kTileBytes,
                               row, blk);
         fence_proxy_async_smem();
         mbar_arrive(&B->kv_full[s]);
-        idx = idx2;
-        jt = jt2;
-        b = b2;
-        g = g2;
+        cur = nxt;
         have = have2;
     }
     cp_async_wait<0>();  // no copy into shared memory outlives the CTA
