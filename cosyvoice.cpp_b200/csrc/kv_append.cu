@@ -18,35 +18,38 @@
 
 namespace cvattn {
 
+// One warp per source row (t, b): the row's position is looked up once, then
+// the warp walks the row's 32-element groups (coalesced 128-byte loads, the
+// iterations independent of each other).
 template <int T>
 __global__ void __launch_bounds__(256) kv_append_kernel(
     uint8_t* __restrict__ cache, int64_t nb1, int64_t nb2, int64_t capacity, int groups_per_row,
     const float* __restrict__ src, int64_t src_nb1, int64_t src_nb2,
     const int32_t* __restrict__ pos, int64_t pos_stride, int n_new, int batch, int* status, RopeDev rope) {
     const int lane = threadIdx.x & 31;
-    const int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int64_t total = (int64_t)n_new * batch * groups_per_row;
-    if (w >= total) return;
-    const int g = (int)(w % groups_per_row);
-    const int64_t r = w / groups_per_row;
-    const int t = (int)(r % n_new);
-    const int b = (int)(r / n_new);
+    const unsigned rw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);  // row (t, b), t fastest
+    if (rw >= (unsigned)n_new * (unsigned)batch) return;
+    const int b = (int)(rw / (unsigned)n_new);
+    const int t = (int)(rw - (unsigned)b * (unsigned)n_new);
     const int p = pos[t + (int64_t)b * pos_stride];
     if (p < 0 || p >= capacity) {
         if (lane == 0) record_status(status, kStatusBadPosition);
         return;
     }
     const float* row = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(src) + t * src_nb1 + b * src_nb2);
-    const int e = g * 32 + lane;
-    float x = row[e];
-    if (rope.n_dims > 0) {
-        int k;
-        bool first;
-        const int pe = rope_pair(rope, e, k, first);
-        if (pe >= 0) x = rope_rotate(x, row[pe], rope_cs(rope, rope_theta(rope, p, k)), first);
+    uint8_t* dst_row = cache + b * nb2 + (int64_t)p * nb1;
+#pragma unroll 4
+    for (int g = 0; g < groups_per_row; ++g) {
+        const int e = g * 32 + lane;
+        float x = row[e];
+        if (rope.n_dims > 0) {
+            int k;
+            bool first;
+            const int pe = rope_pair(rope, e, k, first);
+            if (pe >= 0) x = rope_rotate(x, row[pe], rope_cs(rope, rope_theta(rope, p, k)), first);
+        }
+        quantize_block_warp<T>(x, dst_row + (int64_t)g * group_bytes(T), lane);
     }
-    uint8_t* dst = cache + b * nb2 + (int64_t)p * nb1 + (int64_t)g * group_bytes(T);
-    quantize_block_warp<T>(x, dst, lane);
 }
 
 // Standalone RoPE: rows of row_len floats (row r at x + r * x_nb1f, out + r * out_nb1f;
@@ -96,9 +99,10 @@ cudaError_t launch_kv_append(cudaStream_t stream, const cvattn_tensor& c, const 
     const RopeDev rp = rope ? *rope : RopeDev{0, 0, 1, 1.0f, 1.0f, 1.0f};
     const int row_elems = c.n_heads * c.head_dim;
     const int groups = row_elems / 32;
-    const int64_t warps = (int64_t)n_new * batch * groups;
-    if (warps == 0) return cudaSuccess;
-    const unsigned grid = (unsigned)((warps + 7) / 8);
+    const int64_t rows = (int64_t)n_new * batch;  // one warp per row
+    if (rows == 0) return cudaSuccess;
+    if (rows > 0x7fffffffLL) return cudaErrorInvalidValue;
+    const unsigned grid = (unsigned)((rows + 7) / 8);
     uint8_t* base = static_cast<uint8_t*>(c.data);
 #define CVATTN_APPEND_CASE(T)                                                                              \
     case T:                                                                                                \
