@@ -905,6 +905,17 @@ def run_profile(args, torch) -> None:
         dec, keep = build_cfg4(torch, cv, ctx, kt, vt, gen)
         for _ in range(args.steps):
             dec()
+    elif args.profile == "dit_append":
+        # the DiT step's cache append: 600 rows of 64 batch entries x 1024 f32 into q8_0 K / q4_0 V
+        B, H, P, S = 64, DIT_H, DIT_P, DIT_S
+        kb, kd = cv.alloc_kv(cv.Q8_0, H, D, 1024, B)
+        vb, vd = cv.alloc_kv(cv.Q4_0, H, D, 1024, B)
+        k = torch.randn(B, S, H * D, device="cuda")
+        v = torch.randn(B, S, H * D, device="cuda")
+        pos = torch.arange(P, P + S, dtype=torch.int32, device="cuda")
+        for _ in range(args.steps):
+            cv.kv_append(ctx, kd, k, pos)
+            cv.kv_append(ctx, vd, v, pos)
     else:
         run_flash_secondary(torch, cv, ctx, args, only=args.profile, reps=args.steps)
     torch.cuda.synchronize()
@@ -921,7 +932,7 @@ def main() -> None:
     ap.add_argument("--cpu-baselines", action="store_true",
                     help="time the oracle's CPU restatement on bounded samples of every config and print them")
     ap.add_argument("--profile", choices=["decode", "decode_cfg4", "decode_cfg4_q5_1", "dit", "dit_q8_0_q4_0",
-                                          "prefill"], default=None,
+                                          "prefill", "dit_append"], default=None,
                     help="only launch the named kernel a few times (for an ncu capture); prints nothing")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

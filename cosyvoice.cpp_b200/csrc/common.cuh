@@ -85,36 +85,31 @@ __device__ __forceinline__ float warp_max_abs(float a) {
     return a;
 }
 
-// Signed value of largest magnitude, first occurrence.
+// Signed value of largest magnitude, first occurrence: the largest magnitude by
+// a max reduction, then the lowest lane holding it (a ballot) gives the value.
 __device__ __forceinline__ float warp_signed_absmax(float x, int lane) {
-    float a = fabsf(x);
-    int idx = lane;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        float a2 = __shfl_xor_sync(0xffffffffu, a, o);
-        int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
-        if (a2 > a || (a2 == a && i2 < idx)) { a = a2; idx = i2; }
-    }
+    (void)lane;
+    const float a = warp_max_abs(fabsf(x));
     // ggml keeps max = 0.0f until some |v| > 0: an all-zero block gives +0.0
     if (a == 0.0f) return 0.0f;
-    return __shfl_sync(0xffffffffu, x, idx);
+    const uint32_t hit = __ballot_sync(0xffffffffu, fabsf(x) == a);
+    return __shfl_sync(0xffffffffu, x, __ffs(hit) - 1);
 }
 
-// Minimum / maximum, first occurrence (ties by value resolve to the lower lane).
+// Minimum / maximum, first occurrence (values that compare equal, -0.0 and +0.0,
+// resolve to the lower lane, as ggml's sequential scans do).
 __device__ __forceinline__ void warp_min_max(float x, int lane, float& mn, float& mx) {
+    (void)lane;
     float vmin = x, vmax = x;
-    int imin = lane, imax = lane;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-        float a = __shfl_xor_sync(0xffffffffu, vmin, o);
-        int ia = __shfl_xor_sync(0xffffffffu, imin, o);
-        if (a < vmin || (a == vmin && ia < imin)) { vmin = a; imin = ia; }
-        float b = __shfl_xor_sync(0xffffffffu, vmax, o);
-        int ib = __shfl_xor_sync(0xffffffffu, imax, o);
-        if (b > vmax || (b == vmax && ib < imax)) { vmax = b; imax = ib; }
+        vmin = fminf(vmin, __shfl_xor_sync(0xffffffffu, vmin, o));
+        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
     }
-    mn = vmin;
-    mx = vmax;
+    const uint32_t hmin = __ballot_sync(0xffffffffu, x == vmin);
+    const uint32_t hmax = __ballot_sync(0xffffffffu, x == vmax);
+    mn = __shfl_sync(0xffffffffu, x, __ffs(hmin) - 1);
+    mx = __shfl_sync(0xffffffffu, x, __ffs(hmax) - 1);
 }
 
 __device__ __forceinline__ void store_u16(uint8_t* p, uint16_t v) {

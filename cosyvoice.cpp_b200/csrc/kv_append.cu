@@ -38,17 +38,27 @@ __global__ void __launch_bounds__(256) kv_append_kernel(
     }
     const float* row = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(src) + t * src_nb1 + b * src_nb2);
     uint8_t* dst_row = cache + b * nb2 + (int64_t)p * nb1;
-#pragma unroll 4
-    for (int g = 0; g < groups_per_row; ++g) {
-        const int e = g * 32 + lane;
-        float x = row[e];
+    // eight groups' loads in flight before any of them is quantized
+    constexpr int kBatch = 8;
+    for (int g0 = 0; g0 < groups_per_row; g0 += kBatch) {
+        float x[kBatch];
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) x[i] = g0 + i < groups_per_row ? row[(g0 + i) * 32 + lane] : 0.0f;
         if (rope.n_dims > 0) {
-            int k;
-            bool first;
-            const int pe = rope_pair(rope, e, k, first);
-            if (pe >= 0) x = rope_rotate(x, row[pe], rope_cs(rope, rope_theta(rope, p, k)), first);
+#pragma unroll
+            for (int i = 0; i < kBatch; ++i) {
+                const int e = (g0 + i) * 32 + lane;
+                int k;
+                bool first;
+                const int pe = rope_pair(rope, e, k, first);
+                if (g0 + i < groups_per_row && pe >= 0)
+                    x[i] = rope_rotate(x[i], row[pe], rope_cs(rope, rope_theta(rope, p, k)), first);
+            }
         }
-        quantize_block_warp<T>(x, dst_row + (int64_t)g * group_bytes(T), lane);
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i)
+            if (g0 + i < groups_per_row)  // uniform per warp
+                quantize_block_warp<T>(x[i], dst_row + (int64_t)(g0 + i) * group_bytes(T), lane);
     }
 }
 
