@@ -297,6 +297,7 @@ def run_ours(args, rank: int, world: int, torch, dist) -> dict | None:
         lines.update(run_configs0(torch, cv, ctx))
         lines.update(run_configs1_fixed(torch, cv, ctx))
         lines.update(run_prefill_chunked(torch, cv, ctx))
+        lines.update(run_dit_offload(torch, cv, ctx))
     if rank != 0:
         return None
 
@@ -630,6 +631,85 @@ def run_dit_sharded(torch, cv, ctx, rank: int, world: int, dist, reps: int = DIT
         "flops": flops_total, "frac_bf16_peak": round(tflops / world / peaks["bf16_tflops"], 4),
         "peak_tflops": peaks["bf16_tflops"], "peak_source": peaks["source"], "scaling": "strong",
         "launches_per_ode_step": 3 * DIT_LAYERS}}
+
+
+def run_dit_offload(torch, cv, ctx, reps: int = 10) -> dict:
+    """Slot offload overlapped with the next ODE step, in the reference's schedule:
+    an offloadable step on device slot 0, then a fixed-slot step on slot 1
+    (dit_sched_config, src/cosyvoice-token2wav.cpp:100-167).  One DiT worker: one
+    utterance, CFG batch 2, 22 layers, q8_0 / q4_0 cache object.  A step = per layer
+    the append of 600 K/V rows after the 300 cached prompt rows and the chunk-masked
+    attention over 900 keys.  Timed per pair of steps (CUDA events): the two steps
+    alone; with slot 0 (900 positions of 22 layers) offloaded to pinned host memory
+    on a copy stream while the slot-1 step computes; and the reference's order,
+    offload then wait for it (src/cosyvoice-kv-cache.cpp:148-174 synchronizes), then
+    the slot-1 step."""
+    import ctypes
+    B, H, P, S, Lyr = 2, DIT_H, DIT_P, DIT_S, DIT_LAYERS
+    n_kv = P + S
+    cache = cv.KVCache(ctx, Lyr, D, H, 1024, cv.Q8_0, cv.Q4_0, batch=B, n_slots=2, n_offloaded_slots=1)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(9)
+    ppos = torch.arange(P, dtype=torch.int32, device="cuda")
+    cpos = torch.arange(P, n_kv, dtype=torch.int32, device="cuda")
+    kp = torch.randn(B, P, H * D, device="cuda", generator=gen)
+    k = torch.randn(B, S, H * D, device="cuda", generator=gen)
+    q = torch.randn(B, S, H, D, device="cuda", generator=gen)
+    out = torch.empty_like(q)
+    bounds = list(range(50, S + 1, 50))
+    stream, cstream = torch.cuda.Stream(), torch.cuda.Stream()
+    graphs = []
+    for slot in (0, 1):
+        cache.bind_slot(slot)
+        cache.cur_len = 0
+        for l in range(Lyr):
+            cache.update(l, kp, kp, ppos)  # the cached prompt rows of this slot
+        cache.shift(P)
+        fps = [cv.flash_params(q, cache.tensor(l, slot, 0), cache.tensor(l, slot, 1), n_kv, out,
+                               mask_mode=cv.MASK_CHUNK, chunk_bounds=bounds, chunk_key_offset=P) for l in range(Lyr)]
+
+        def step(s, fps=fps):
+            sp = s.cuda_stream
+            for l in range(Lyr):
+                cache.update(l, k, k, cpos, stream=sp)  # into the slot bound at capture
+                cv.check(cv.lib.cvattn_flash(ctx.handle, sp, ctypes.byref(fps[l])), "dit step")
+
+        graphs.append((_graph_of(torch, stream, step), fps))
+    cache.offload_slot(0, n_kv, stream=cstream)  # allocates the pinned host slot once
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def run(mode):
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            stream.wait_stream(cstream)       # slot 0 is rewritten only after its last offload read it
+            with torch.cuda.stream(stream):
+                graphs[0][0].replay()           # offloadable step: device slot 0
+            if mode == "overlap":
+                cstream.wait_stream(stream)
+                cache.offload_slot(0, n_kv, stream=cstream)
+            elif mode == "serial":
+                cache.offload_slot(0, n_kv, stream=stream)
+                stream.synchronize()
+            with torch.cuda.stream(stream):
+                graphs[1][0].replay()           # fixed-slot step: device slot 1
+        stream.wait_stream(cstream)
+        e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    alone, overlap, serial = run("alone"), run("overlap"), run("serial")
+    nbytes = Lyr * B * n_kv * (cv.row_size(cv.Q8_0, H * D) + cv.row_size(cv.Q4_0, H * D))
+    del graphs
+    cache.close()
+    _check_status(ctx, "the offload overlap")
+    return {"dit_offload": {
+        "what": "one DiT worker (utterance x CFG 2, 22 layers, q8_0/q4_0): an offloadable step on slot 0 then a "
+                "fixed-slot step; slot 0 offloaded to pinned host on a copy stream during the second step, against "
+                "the two steps alone and the reference's offload-then-synchronize order",
+        "slot_bytes": nbytes, "two_steps_ms": round(alone, 3), "two_steps_with_offload_overlapped_ms": round(overlap, 3),
+        "offload_then_sync_ms": round(serial, 3)}}
 
 
 def run_flash_secondary(torch, cv, ctx, args, only: str | None = None, reps: int = 10) -> dict:
