@@ -110,13 +110,34 @@ struct Item {
     bool active[2];
 };
 
-// Items are ordered longest first (query tile index descending) so the
-// causal / chunk-masked tail finishes together; for G = 1 the pairs of one
-// head stay adjacent instead (they read the same K/V).
+// Pairing: for an even G, two query heads of one KV group at the same query
+// tile; for G = 1 and odd G, two consecutive query tiles of one head (an odd G
+// paired by heads would leave one item in (G + 1) / 2 half empty: 1 in 4 for
+// Qwen2's G = 7).  Items are ordered longest first (query tile index
+// descending) so the causal / chunk-masked tail finishes together; for G = 1 the
+// pairs of one head stay adjacent instead (they read the same K/V).
+__device__ __forceinline__ bool heads_paired(const Params& p) { return p.G >= 2 && (p.G & 1) == 0; }
+
 __device__ __forceinline__ Item item_at(const Params& p, int idx) {
     Item it;
     const int n_qt = (p.n_q + BM - 1) / BM;
     const int Hkv = p.Hq / p.G;
+    if (!heads_paired(p) && p.G >= 3) {
+        // consecutive query tiles of one head; pairs longest first, every head at a pair index
+        // next to each other, so the G heads of a KV group share its K/V through L2
+        const int qpairs = (n_qt + 1) / 2;
+        const int per_qp = p.batch * p.Hq;
+        const int qp = qpairs - 1 - idx / per_qp;
+        const int r = idx % per_qp;
+        it.h[0] = it.h[1] = r % p.Hq;
+        it.g = it.h[0] / p.G;
+        it.b = r / p.Hq;
+        it.qt[0] = 2 * qp;
+        it.qt[1] = 2 * qp + 1;
+        it.active[0] = true;
+        it.active[1] = it.qt[1] < n_qt;
+        return it;
+    }
     if (p.G >= 2) {
         const int pairs = (p.G + 1) / 2;
         const int per_qt = p.batch * Hkv * pairs;
@@ -150,7 +171,7 @@ __device__ __forceinline__ Item item_at(const Params& p, int idx) {
 __device__ __forceinline__ int n_items(const Params& p) {
     const int n_qt = (p.n_q + BM - 1) / BM;
     const int Hkv = p.Hq / p.G;
-    if (p.G >= 2) return n_qt * p.batch * Hkv * ((p.G + 1) / 2);
+    if (heads_paired(p)) return n_qt * p.batch * Hkv * ((p.G + 1) / 2);
     return ((n_qt + 1) / 2) * p.batch * p.Hq;
 }
 

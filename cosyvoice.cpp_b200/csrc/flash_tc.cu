@@ -115,9 +115,11 @@ cudaError_t launch_flash(cudaStream_t stream, const cvattn_flash_params& a, int*
         // persistent kernel: one CTA per SM over the query-tile pairs
         const int num_sms = current_sm_count();
         if (num_sms <= 0) return cudaErrorInvalidDevice;
+        // the item count of fp::n_items: head pairs for an even G, query-tile pairs otherwise
         const long n_qt = (a.n_q + BM - 1) / BM;
-        const long items = p.G >= 2 ? n_qt * a.batch * (a.n_q_heads / p.G) * ((p.G + 1) / 2)
-                                    : ((n_qt + 1) / 2) * a.batch * a.n_q_heads;
+        const bool heads_paired = p.G >= 2 && (p.G & 1) == 0;
+        const long items = heads_paired ? n_qt * a.batch * (a.n_q_heads / p.G) * ((p.G + 1) / 2)
+                                        : ((n_qt + 1) / 2) * a.batch * a.n_q_heads;
         if (items <= 0) return cudaSuccess;
         const dim3 grid_p((unsigned)(items < num_sms ? items : num_sms));
         switch (a.k.type) {

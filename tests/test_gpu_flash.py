@@ -212,3 +212,18 @@ def test_dit_cached_many_items_per_cta(ctx, cv, cuda, oracle, fk):
     cm = oracle.mask_bits_to_f32(oracle.chunk_mask(S, bounds))
     mask = np.concatenate([np.zeros((S, P), np.float32), cm], axis=1)[None]
     check(out, reference(oracle, cv.F16, cv.F16, kq, vq, q, n_kv, H, mask), "dit cached many items")
+
+
+@pytest.mark.parametrize("Hq", [2, 4, 6, 16])
+def test_prefill_causal_group_sizes(ctx, cv, cuda, oracle, fk, Hq):
+    """G = 1, 2, 3, 8 query heads per KV head: head pairs (even G) and query-tile pairs (G = 1, odd G)."""
+    torch = cuda
+    rng = np.random.default_rng(100 + Hq)
+    B, Hkv, n_q, cur = 2, 2, 300, 40
+    n_kv = cur + n_q
+    kq, kb, kd = make_kv(cv, cuda, oracle, cv.Q8_0, n_kv, Hkv, B, rng)
+    vq, vb, vd = make_kv(cv, cuda, oracle, cv.Q4_0, n_kv, Hkv, B, rng)
+    q = rng.standard_normal((B, n_q, Hq, D)).astype(np.float32)
+    out = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, n_kv, mask_mode=cv.MASK_CAUSAL, flags=fk).cpu().numpy()
+    mask = oracle.mask_bits_to_f32(oracle.causal_mask(n_q, n_kv))[None]
+    check(out, reference(oracle, cv.Q8_0, cv.Q4_0, kq, vq, q, n_kv, Hkv, mask), f"Hq={Hq}")
