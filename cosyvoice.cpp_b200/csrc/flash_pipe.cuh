@@ -53,6 +53,7 @@ constexpr float kRescaleP = 256.0f;  // 2^kRescaleThreshold
 #endif
 constexpr bool kExpPoly = CVATTN_FLASH_EXP_POLY != 0;  // part of the exponentials on the FMA pipe
 
+
 // shared memory (offsets from a 1024-aligned base)
 constexpr int kTileBytes = kBN * D * 2;              // 8 KB
 constexpr int kQOff = 0;                             // 2 x 16 KB
