@@ -158,7 +158,9 @@ def _barrier(torch, dist):
 
 
 def _graph_of(torch, stream, fn, warm: int = 3):
-    """Warm fn up on `stream`, then capture one call of it in a CUDA graph."""
+    """Warm fn up on `stream`, then capture one call of it in a CUDA graph.  The inputs
+    were made on the default stream: wait for them first."""
+    torch.cuda.synchronize()
     with torch.cuda.stream(stream):
         for _ in range(warm):
             fn(stream)
