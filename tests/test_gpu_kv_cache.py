@@ -114,6 +114,7 @@ def test_decode_call_neither_syncs_nor_allocates(ctx, cv, cuda, oracle):
     q = torch.tensor(rng.standard_normal((1, 1, Hq, D)).astype(np.float32), device="cuda")
     out = torch.zeros_like(q)
     s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())  # the rows and buffers above were written on the default stream
     with torch.cuda.stream(s):
         cache.update(0, knew, vnew, pos, stream=s)
         cache.attention(0, q, out=out, stream=s)   # warm-up outside the capture
@@ -238,6 +239,7 @@ def test_offload_load_round_trip_reference_layout(ctx, cv, cuda, oracle, other_s
     expect = b"".join(kq.tobytes() + vq.tobytes() for kq, vq in written)
     s1 = torch.cuda.Stream()
     s2 = torch.cuda.Stream() if other_stream else s1
+    s1.wait_stream(torch.cuda.current_stream())  # the slot's rows were appended on the default stream
     cache.offload_slot(1, n, stream=s1)      # enqueued only: no host synchronization
     host, length = cache.offloaded_slot(1)
     assert length == n and host.tobytes() == expect
@@ -248,6 +250,7 @@ def test_offload_load_round_trip_reference_layout(ctx, cv, cuda, oracle, other_s
         cache.update(layer, junk, junk, pos)
     cache.cur_len = 5
     cache.bind_slot(1)                       # load_cache writes the bound slot
+    s2.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s2):
         cache.load_slot(1, stream=s2)
     assert cache.cur_len == n               # load restores cur_len
