@@ -66,9 +66,16 @@ constexpr int kRawOff = kSmemBytes;                  // staged producer: raw row
 __host__ __device__ constexpr bool is_block_quant(int t) {
     return t == kQ4_0 || t == kQ4_1 || t == kQ5_0 || t == kQ5_1 || t == kQ8_0;
 }
-// Bytes of the raw K and V head rows of one 64-key tile (staged producer).
+// Width in bytes of the TMA box that holds one raw head row of type t (staged
+// producer, TMA form): the row starts 4-byte aligned, the box at the 16-byte
+// boundary at or below it, so it spans the row plus up to 12 leading bytes.
+__host__ __device__ constexpr int raw_box_bytes(int t) {
+    return (2 * group_bytes(t) + ((2 * group_bytes(t)) % 16 ? 12 : 0) + 15) / 16 * 16;
+}
+// Bytes of the raw K and V head rows of one 64-key tile (staged producer): the
+// larger of the packed cp.async layout and the TMA box layout.
 __host__ __device__ constexpr int raw_tile_bytes(int kt, int vt) {
-    return (kBN * 2 * (group_bytes(kt) + group_bytes(vt)) + 127) / 128 * 128;
+    return kBN * (raw_box_bytes(kt) + raw_box_bytes(vt));
 }
 // Dynamic shared memory of flash_pipe_kernel<KT, VT>.
 __host__ __device__ constexpr int smem_bytes(int kt, int vt) {
@@ -83,6 +90,7 @@ struct Bars {
     uint64_t p_ready[2][2];
     uint64_t o_done[2][2];   // O(T) commits o_done[x][T & 1]
     uint64_t o_free[2];
+    uint64_t raw_full[2];    // staged producer, TMA form: raw tile n landed in buffer n & 1
     uint32_t tmem_base;
     int err;
 };
@@ -338,12 +346,18 @@ __device__ __forceinline__ void convert_block_f16(const uint8_t* g, bool valid, 
 }
 
 // The producer role for block-quantized K and V (128 threads, r = 0..127).
-// Tiles are produced in the order the MMA issuers consume them.
-template <int KT, int VT>
-__device__ __forceinline__ void produce_staged(const Params& p, uint8_t* smem, Bars* B, int total, int r) {
+// Tiles are produced in the order the MMA issuers consume them.  kTma: the raw
+// rows of a tile arrive as two TMA tensor loads (byte maps, boxes of
+// raw_box_bytes x 64 rows starting at the 16-byte boundary below the head's
+// row) issued by one thread; otherwise as coalesced 4-byte cp.async by all 128.
+template <int KT, int VT, bool kTma>
+__device__ __forceinline__ void produce_staged(const Params& p, uint8_t* smem, Bars* B, int total, int r,
+                                               const CUtensorMap* kmap, const CUtensorMap* vmap) {
     constexpr int HBK = 2 * group_bytes(KT), HBV = 2 * group_bytes(VT);  // bytes of one head row
     constexpr int WK = HBK / 4, WV = HBV / 4;
     constexpr int RB = raw_tile_bytes(KT, VT);
+    // row pitch of the raw tile in shared memory
+    constexpr int PK = kTma ? raw_box_bytes(KT) : HBK, PV = kTma ? raw_box_bytes(VT) : HBV;
     constexpr int kBar = 1;  // named barrier of the 128 producer threads
     uint8_t* raw0 = smem + kRawOff;
     // tile cursor: item idx (its batch entry, KV head and key-tile count) and tile j;
@@ -370,7 +384,15 @@ __device__ __forceinline__ void produce_staged(const Params& p, uint8_t* smem, B
         c.idx += gridDim.x;
         return find_item(c);
     };
-    auto issue = [&](const Cursor& c, uint8_t* dst) {
+    auto issue = [&](const Cursor& c, uint8_t* dst, int buf) {
+        if constexpr (kTma) {
+            if (r == 0) {
+                mbar_arrive_expect_tx(&B->raw_full[buf], (uint32_t)(kBN * (PK + PV)));
+                tc::tma_load_3d(dst, kmap, (c.g * HBK) & ~15, c.j * kBN, c.b, &B->raw_full[buf]);
+                tc::tma_load_3d(dst + kBN * PK, vmap, (c.g * HBV) & ~15, c.j * kBN, c.b, &B->raw_full[buf]);
+            }
+            return;
+        }
         const uint8_t* kb = p.k + (int64_t)c.b * p.k_nb2 + (int64_t)c.g * HBK + (int64_t)c.j * kBN * p.k_nb1;
         const uint8_t* vb = p.v + (int64_t)c.b * p.v_nb2 + (int64_t)c.g * HBV + (int64_t)c.j * kBN * p.v_nb1;
         const int rows = min(kBN, p.n_kv - c.j * kBN);
@@ -387,36 +409,71 @@ __device__ __forceinline__ void produce_staged(const Params& p, uint8_t* smem, B
         }
         cp_async_commit();
     };
+    if constexpr (kTma) {
+        if (r == 0) {
+            tc::prefetch_tmap(kmap);
+            tc::prefetch_tmap(vmap);
+        }
+    }
+    uint32_t issued = 0, landed = 0;  // TMA form: tiles issued / seen landed (thread 0's count)
     Cursor cur{(int)blockIdx.x, 0, 0, 0, 0};
     bool have = find_item(cur);
-    if (have) issue(cur, raw0);
+    if (have) {
+        issue(cur, raw0, 0);
+        ++issued;
+    }
     const int row = r & (kBN - 1), blk = r >> 6;
     for (uint32_t n = 0; have; ++n) {
         Cursor nxt = cur;
         const bool have2 = advance(nxt);
         prod_bar(kBar, 128);  // tile n - 1 is converted: its raw buffer takes tile n + 1
-        if (have2) {
-            issue(nxt, raw0 + ((n + 1) & 1) * RB);
-            cp_async_wait<1>();
+        bool ok = true;
+        if constexpr (kTma) {
+            if (have2) {
+                if (r == 0) fence_proxy_async_smem();  // the generic reads of tile n - 1 precede the TMA write
+                issue(nxt, raw0 + ((n + 1) & 1) * RB, (int)((n + 1) & 1));
+                ++issued;
+            }
+            ok = wait_or_err(&B->raw_full[n & 1], (n >> 1) & 1, &B->err, p.status, 14);
+            if (ok) ++landed;
         } else {
-            cp_async_wait<0>();
+            if (have2) {
+                issue(nxt, raw0 + ((n + 1) & 1) * RB, 0);
+                cp_async_wait<1>();
+            } else {
+                cp_async_wait<0>();
+            }
         }
         const int s = n % kStages;
         const uint32_t use = n / kStages;
-        const bool ok = use == 0 || wait_or_err(&B->kv_empty[s], (use - 1) & 1, &B->err, p.status, 5);
+        ok = ok && (use == 0 || wait_or_err(&B->kv_empty[s], (use - 1) & 1, &B->err, p.status, 5));
         // every thread's copies of tile n have landed and stage s is free (or all stop together)
         if (!prod_bar_and(kBar, 128, ok)) break;
         const uint8_t* raw = raw0 + (n & 1) * RB;
         const bool valid = cur.j * kBN + row < p.n_kv;
-        convert_block_f16<KT>(raw + row * HBK + blk * group_bytes(KT), valid, smem + kKOff + s * kTileBytes, row, blk);
-        convert_block_f16<VT>(raw + kBN * HBK + row * HBV + blk * group_bytes(VT), valid, smem + kVOff + s * kTileBytes,
-                              row, blk);
+        const int ok_ = kTma ? ((cur.g * HBK) & 15) : 0, ov_ = kTma ? ((cur.g * HBV) & 15) : 0;
+        convert_block_f16<KT>(raw + row * PK + ok_ + blk * group_bytes(KT), valid, smem + kKOff + s * kTileBytes, row,
+                              blk);
+        convert_block_f16<VT>(raw + kBN * PK + row * PV + ov_ + blk * group_bytes(VT), valid,
+                              smem + kVOff + s * kTileBytes, row, blk);
         fence_proxy_async_smem();
         mbar_arrive(&B->kv_full[s]);
         cur = nxt;
         have = have2;
     }
-    cp_async_wait<0>();  // no copy into shared memory outlives the CTA
+    if constexpr (kTma) {
+        // no TMA write into shared memory outlives the CTA: thread 0 waits (bounded) for the
+        // tiles it issued that were not seen landing (at most two, in different buffers)
+        if (r == 0) {
+            for (uint32_t t = landed; t < issued; ++t) {
+                const uint64_t t0 = global_timer_ns();
+                while (!mbar_try_wait_hint(&B->raw_full[t & 1], (t >> 1) & 1, 1000u))
+                    if (global_timer_ns() - t0 > kWaitBudgetNs) break;
+            }
+        }
+    } else {
+        cp_async_wait<0>();  // no copy into shared memory outlives the CTA
+    }
 }
 
 template <int KT, int VT>
@@ -440,6 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int x = 0; x < 2; ++x) {
             mbar_init(&B->q_full[x], 128);
             mbar_init(&B->o_free[x], 128);
+            mbar_init(&B->raw_full[x], 1);
             for (int b = 0; b < 2; ++b) {
                 mbar_init(&B->s_full[x][b], 1);
                 mbar_init(&B->p_ready[x][b], 128);
@@ -612,7 +670,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = tid - kProdWarp0 * 32;  // 0..127 = key row of the tile
         if constexpr (is_block_quant(KT) && is_block_quant(VT)) {
             if (p.staged) {
-                produce_staged<KT, VT>(p, smem, B, total, r);
+                if (p.staged == 2) produce_staged<KT, VT, true>(p, smem, B, total, r, &kmap, &vmap);
+                else produce_staged<KT, VT, false>(p, smem, B, total, r, &kmap, &vmap);
                 goto producer_done;
             }
         }

@@ -42,6 +42,22 @@ static bool make_kv_map(CUtensorMap* map, const cvattn_tensor& t, int n_kv, int 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Block-quantized KV tensor as raw bytes for the staged producer's TMA form:
+// a 3-D byte map {row bytes, n_kv positions, batch}, box of box_bytes x 64
+// positions, no swizzle; positions >= n_kv and bytes past the row read as zero.
+static bool make_raw_map(CUtensorMap* map, const cvattn_tensor& t, int n_kv, int batch, int box_bytes) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)t.n_heads * type_row_bytes(t.type, t.head_dim), (cuuint64_t)n_kv,
+                                (cuuint64_t)batch};
+    const cuuint64_t strides[2] = {(cuuint64_t)t.nb1, (cuuint64_t)t.nb2};
+    const cuuint32_t box[3] = {(cuuint32_t)box_bytes, (cuuint32_t)fp::kBN, 1};
+    const cuuint32_t estride[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, t.data, dims, strides, box, estride,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace fa
 
 bool flash_supported(int k_type, int v_type, int head_dim, int n_q_heads, int n_kv_heads) {
@@ -111,6 +127,14 @@ cudaError_t launch_flash(cudaStream_t stream, const cvattn_flash_params& a, int*
     p.staged = fp::is_block_quant(a.k.type) && fp::is_block_quant(a.v.type) &&
                ((reinterpret_cast<uintptr_t>(a.k.data) | reinterpret_cast<uintptr_t>(a.v.data)) & 3) == 0 &&
                ((a.k.nb1 | a.k.nb2 | a.v.nb1 | a.v.nb2) & 3) == 0;
+    // its TMA form: 16-byte aligned bases and strides (the box x coordinate is the
+    // 16-byte boundary below the head's row) and rows at least one box wide
+    if (p.staged && aligned && a.n_kv > 0 && !(a.flags & CVATTN_FLASH_ONE_TILE)) {
+        const int bk = fp::raw_box_bytes(a.k.type), bv = fp::raw_box_bytes(a.v.type);
+        if ((long)a.k.n_heads * p.k_head_bytes >= bk && (long)a.v.n_heads * p.v_head_bytes >= bv &&
+            make_raw_map(&km, a.k, a.n_kv, a.batch, bk) && make_raw_map(&vm, a.v, a.n_kv, a.batch, bv))
+            p.staged = 2;
+    }
     if (!(a.flags & CVATTN_FLASH_ONE_TILE)) {
         // persistent kernel: one CTA per SM over the query-tile pairs
         const int num_sms = current_sm_count();

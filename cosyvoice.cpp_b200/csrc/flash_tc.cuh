@@ -70,7 +70,7 @@ struct Params {
     int bounds[CVATTN_MAX_CHUNK_BOUNDS];
     int key_offset, row_offset;
     int use_tma;
-    int staged;  // block-quantized K and V with 4-byte aligned rows: the staged producer (flash_pipe)
+    int staged;  // block-quantized K and V: the staged producer (flash_pipe); 2 = its TMA form
     int* status;
 };
 

@@ -227,3 +227,24 @@ def test_prefill_causal_group_sizes(ctx, cv, cuda, oracle, fk, Hq):
     out = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, n_kv, mask_mode=cv.MASK_CAUSAL, flags=fk).cpu().numpy()
     mask = oracle.mask_bits_to_f32(oracle.causal_mask(n_q, n_kv))[None]
     check(out, reference(oracle, cv.Q8_0, cv.Q4_0, kq, vq, q, n_kv, Hkv, mask), f"Hq={Hq}")
+
+
+QUANT = ["q8_0", "q5_1", "q5_0", "q4_1", "q4_0"]
+
+
+@pytest.mark.parametrize("kname", QUANT)
+@pytest.mark.parametrize("vname", QUANT)
+def test_staged_tma_form_type_pairs(ctx, cv, cuda, oracle, kname, vname):
+    """4 KV heads make every block-quantized row a multiple of 16 bytes, so the
+    persistent kernel's producer fetches the raw rows with TMA byte boxes that
+    start at the 16-byte boundary below each head (head offsets 0, 4, 8, 12
+    bytes for q8_0); 201 keys leave a ragged last tile read past n_kv."""
+    torch = cuda
+    kt, vt = cv.TYPE_BY_NAME[kname], cv.TYPE_BY_NAME[vname]
+    rng = np.random.default_rng(kt * 17 + vt + 5)
+    B, Hq, Hkv, n_q, n_kv = 2, 8, 4, 130, 201
+    kq, kb, kd = make_kv(cv, cuda, oracle, kt, n_kv, Hkv, B, rng, cap=n_kv + 7)
+    vq, vb, vd = make_kv(cv, cuda, oracle, vt, n_kv, Hkv, B, rng, cap=n_kv + 7)
+    q = rng.standard_normal((B, n_q, Hq, D)).astype(np.float32)
+    out = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, n_kv).cpu().numpy()
+    check(out, reference(oracle, kt, vt, kq, vq, q, n_kv, Hkv), f"{kname}/{vname}")
