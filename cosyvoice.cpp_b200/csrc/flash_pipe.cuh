@@ -345,19 +345,33 @@ __device__ __forceinline__ void convert_block_f16(const uint8_t* g, bool valid, 
             make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
 }
 
+// Forms of the staged producer (Params::staged).
+constexpr int kStagedCpAsync = 1;  // 4-byte cp.async of each head row by all 128 threads
+constexpr int kStagedBoxes = 2;    // rows 16-byte aligned: TMA byte boxes around the head's row
+constexpr int kStagedChunk = 3;    // contiguous rows: one bulk copy of the tile's whole rows
+// Largest raw tile of the chunk form (whole K and V rows of 64 keys).
+constexpr int kChunkRawMax = 48 * 1024;
+
 // The producer role for block-quantized K and V (128 threads, r = 0..127).
-// Tiles are produced in the order the MMA issuers consume them.  kTma: the raw
-// rows of a tile arrive as two TMA tensor loads (byte maps, boxes of
-// raw_box_bytes x 64 rows starting at the 16-byte boundary below the head's
-// row) issued by one thread; otherwise as coalesced 4-byte cp.async by all 128.
-template <int KT, int VT, bool kTma>
+// Tiles are produced in the order the MMA issuers consume them, one raw tile
+// ahead in two raw buffers.  The raw rows arrive in one of three forms:
+//   kStagedCpAsync: coalesced 4-byte cp.async of the head rows by all 128 threads;
+//   kStagedBoxes:   two TMA tensor loads by one thread (byte maps, boxes of
+//                   raw_box_bytes x 64 rows from the 16-byte boundary below the head);
+//   kStagedChunk:   the tile's 64 rows are contiguous in memory, so one thread
+//                   copies them whole (all KV heads) with cp.async.bulk, and the
+//                   last <= 12 bytes of a ragged tile with 4-byte cp.async.
+template <int KT, int VT, int kForm>
 __device__ __forceinline__ void produce_staged(const Params& p, uint8_t* smem, Bars* B, int total, int r,
                                                const CUtensorMap* kmap, const CUtensorMap* vmap) {
     constexpr int HBK = 2 * group_bytes(KT), HBV = 2 * group_bytes(VT);  // bytes of one head row
     constexpr int WK = HBK / 4, WV = HBV / 4;
-    constexpr int RB = raw_tile_bytes(KT, VT);
-    // row pitch of the raw tile in shared memory
-    constexpr int PK = kTma ? raw_box_bytes(KT) : HBK, PV = kTma ? raw_box_bytes(VT) : HBV;
+    constexpr bool kBoxes = kForm == kStagedBoxes, kChunk = kForm == kStagedChunk;
+    // raw buffer size, K part size, and the row pitch of the raw tile in shared memory
+    const int RB = kChunk ? p.raw_bytes : raw_tile_bytes(KT, VT);
+    const int KB = kChunk ? p.raw_k_bytes : kBN * (kBoxes ? raw_box_bytes(KT) : HBK);
+    const int PK = kChunk ? (int)p.k_nb1 : (kBoxes ? raw_box_bytes(KT) : HBK);
+    const int PV = kChunk ? (int)p.v_nb1 : (kBoxes ? raw_box_bytes(VT) : HBV);
     constexpr int kBar = 1;  // named barrier of the 128 producer threads
     uint8_t* raw0 = smem + kRawOff;
     // tile cursor: item idx (its batch entry, KV head and key-tile count) and tile j;
@@ -385,37 +399,51 @@ __device__ __forceinline__ void produce_staged(const Params& p, uint8_t* smem, B
         return find_item(c);
     };
     auto issue = [&](const Cursor& c, uint8_t* dst, int buf) {
-        if constexpr (kTma) {
-            if (r == 0) {
-                mbar_arrive_expect_tx(&B->raw_full[buf], (uint32_t)(kBN * (PK + PV)));
-                tc::tma_load_3d(dst, kmap, (c.g * HBK) & ~15, c.j * kBN, c.b, &B->raw_full[buf]);
-                tc::tma_load_3d(dst + kBN * PK, vmap, (c.g * HBV) & ~15, c.j * kBN, c.b, &B->raw_full[buf]);
-            }
-            return;
-        }
-        const uint8_t* kb = p.k + (int64_t)c.b * p.k_nb2 + (int64_t)c.g * HBK + (int64_t)c.j * kBN * p.k_nb1;
-        const uint8_t* vb = p.v + (int64_t)c.b * p.v_nb2 + (int64_t)c.g * HBV + (int64_t)c.j * kBN * p.v_nb1;
         const int rows = min(kBN, p.n_kv - c.j * kBN);
+        if constexpr (kBoxes) {
+            if (r == 0) {
+                mbar_arrive_expect_tx(&B->raw_full[buf], (uint32_t)RB);
+                tc::tma_load_3d(dst, kmap, (c.g * HBK) & ~15, c.j * kBN, c.b, &B->raw_full[buf]);
+                tc::tma_load_3d(dst + KB, vmap, (c.g * HBV) & ~15, c.j * kBN, c.b, &B->raw_full[buf]);
+            }
+        } else if constexpr (kChunk) {
+            if (r == 0) {
+                const uint8_t* ks = p.k + (int64_t)c.b * p.k_nb2 + (int64_t)c.j * kBN * p.k_nb1;
+                const uint8_t* vs = p.v + (int64_t)c.b * p.v_nb2 + (int64_t)c.j * kBN * p.v_nb1;
+                const uint32_t kbytes = (uint32_t)rows * (uint32_t)p.k_nb1, vbytes = (uint32_t)rows * (uint32_t)p.v_nb1;
+                const uint32_t kb16 = kbytes & ~15u, vb16 = vbytes & ~15u;
+                mbar_arrive_expect_tx(&B->raw_full[buf], kb16 + vb16);
+                bulk_g2s(dst, ks, kb16, &B->raw_full[buf]);
+                bulk_g2s(dst + KB, vs, vb16, &B->raw_full[buf]);
+                for (uint32_t o = kb16; o < kbytes; o += 4) cp_async4(dst + o, ks + o);
+                for (uint32_t o = vb16; o < vbytes; o += 4) cp_async4(dst + KB + o, vs + o);
+            }
+            cp_async_commit();
+        } else {
+            const uint8_t* kb = p.k + (int64_t)c.b * p.k_nb2 + (int64_t)c.g * HBK + (int64_t)c.j * kBN * p.k_nb1;
+            const uint8_t* vb = p.v + (int64_t)c.b * p.v_nb2 + (int64_t)c.g * HBV + (int64_t)c.j * kBN * p.v_nb1;
 #pragma unroll 4
-        for (int w = r; w < kBN * WK; w += 128) {
-            const int row = w / WK, wi = w - row * WK;
-            if (row < rows) cp_async4(dst + row * HBK + 4 * wi, kb + (int64_t)row * p.k_nb1 + 4 * wi);
-        }
-        uint8_t* vdst = dst + kBN * HBK;
+            for (int w = r; w < kBN * WK; w += 128) {
+                const int row = w / WK, wi = w - row * WK;
+                if (row < rows) cp_async4(dst + row * HBK + 4 * wi, kb + (int64_t)row * p.k_nb1 + 4 * wi);
+            }
+            uint8_t* vdst = dst + kBN * HBK;
 #pragma unroll 4
-        for (int w = r; w < kBN * WV; w += 128) {
-            const int row = w / WV, wi = w - row * WV;
-            if (row < rows) cp_async4(vdst + row * HBV + 4 * wi, vb + (int64_t)row * p.v_nb1 + 4 * wi);
+            for (int w = r; w < kBN * WV; w += 128) {
+                const int row = w / WV, wi = w - row * WV;
+                if (row < rows) cp_async4(vdst + row * HBV + 4 * wi, vb + (int64_t)row * p.v_nb1 + 4 * wi);
+            }
+            cp_async_commit();
         }
-        cp_async_commit();
     };
-    if constexpr (kTma) {
+    if constexpr (kBoxes) {
         if (r == 0) {
             tc::prefetch_tmap(kmap);
             tc::prefetch_tmap(vmap);
         }
     }
-    uint32_t issued = 0, landed = 0;  // TMA form: tiles issued / seen landed (thread 0's count)
+    constexpr bool kMbar = kBoxes || kChunk;  // raw tiles land on raw_full[buf]
+    uint32_t issued = 0, landed = 0;          // raw_full forms: tiles issued / seen landed (thread 0's count)
     Cursor cur{(int)blockIdx.x, 0, 0, 0, 0};
     bool have = find_item(cur);
     if (have) {
@@ -428,21 +456,18 @@ __device__ __forceinline__ void produce_staged(const Params& p, uint8_t* smem, B
         const bool have2 = advance(nxt);
         prod_bar(kBar, 128);  // tile n - 1 is converted: its raw buffer takes tile n + 1
         bool ok = true;
-        if constexpr (kTma) {
-            if (have2) {
-                if (r == 0) fence_proxy_async_smem();  // the generic reads of tile n - 1 precede the TMA write
-                issue(nxt, raw0 + ((n + 1) & 1) * RB, (int)((n + 1) & 1));
-                ++issued;
-            }
+        if (have2) {
+            if (kMbar && r == 0) fence_proxy_async_smem();  // the generic reads of tile n - 1 precede the async writes
+            issue(nxt, raw0 + ((n + 1) & 1) * RB, (int)((n + 1) & 1));
+            ++issued;
+        }
+        if constexpr (kMbar) {
             ok = wait_or_err(&B->raw_full[n & 1], (n >> 1) & 1, &B->err, p.status, 14);
             if (ok) ++landed;
-        } else {
-            if (have2) {
-                issue(nxt, raw0 + ((n + 1) & 1) * RB, 0);
-                cp_async_wait<1>();
-            } else {
-                cp_async_wait<0>();
-            }
+        }
+        if constexpr (!kBoxes) {  // this thread's cp.async of tile n (the chunk form's tail)
+            if (have2) cp_async_wait<1>();
+            else cp_async_wait<0>();
         }
         const int s = n % kStages;
         const uint32_t use = n / kStages;
@@ -451,18 +476,20 @@ __device__ __forceinline__ void produce_staged(const Params& p, uint8_t* smem, B
         if (!prod_bar_and(kBar, 128, ok)) break;
         const uint8_t* raw = raw0 + (n & 1) * RB;
         const bool valid = cur.j * kBN + row < p.n_kv;
-        const int ok_ = kTma ? ((cur.g * HBK) & 15) : 0, ov_ = kTma ? ((cur.g * HBV) & 15) : 0;
-        convert_block_f16<KT>(raw + row * PK + ok_ + blk * group_bytes(KT), valid, smem + kKOff + s * kTileBytes, row,
+        // the head's first byte in a raw row
+        const int hk = kChunk ? cur.g * HBK : (kBoxes ? ((cur.g * HBK) & 15) : 0);
+        const int hv = kChunk ? cur.g * HBV : (kBoxes ? ((cur.g * HBV) & 15) : 0);
+        convert_block_f16<KT>(raw + row * PK + hk + blk * group_bytes(KT), valid, smem + kKOff + s * kTileBytes, row,
                               blk);
-        convert_block_f16<VT>(raw + kBN * PK + row * PV + ov_ + blk * group_bytes(VT), valid,
+        convert_block_f16<VT>(raw + KB + row * PV + hv + blk * group_bytes(VT), valid,
                               smem + kVOff + s * kTileBytes, row, blk);
         fence_proxy_async_smem();
         mbar_arrive(&B->kv_full[s]);
         cur = nxt;
         have = have2;
     }
-    if constexpr (kTma) {
-        // no TMA write into shared memory outlives the CTA: thread 0 waits (bounded) for the
+    if constexpr (kMbar) {
+        // no async write into shared memory outlives the CTA: thread 0 waits (bounded) for the
         // tiles it issued that were not seen landing (at most two, in different buffers)
         if (r == 0) {
             for (uint32_t t = landed; t < issued; ++t) {
@@ -471,9 +498,8 @@ __device__ __forceinline__ void produce_staged(const Params& p, uint8_t* smem, B
                     if (global_timer_ns() - t0 > kWaitBudgetNs) break;
             }
         }
-    } else {
-        cp_async_wait<0>();  // no copy into shared memory outlives the CTA
     }
+    if constexpr (!kBoxes) cp_async_wait<0>();  // no copy into shared memory outlives the CTA
 }
 
 template <int KT, int VT>
@@ -670,8 +696,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = tid - kProdWarp0 * 32;  // 0..127 = key row of the tile
         if constexpr (is_block_quant(KT) && is_block_quant(VT)) {
             if (p.staged) {
-                if (p.staged == 2) produce_staged<KT, VT, true>(p, smem, B, total, r, &kmap, &vmap);
-                else produce_staged<KT, VT, false>(p, smem, B, total, r, &kmap, &vmap);
+                if (p.staged == kStagedBoxes) produce_staged<KT, VT, kStagedBoxes>(p, smem, B, total, r, &kmap, &vmap);
+                else if (p.staged == kStagedChunk) produce_staged<KT, VT, kStagedChunk>(p, smem, B, total, r, &kmap, &vmap);
+                else produce_staged<KT, VT, kStagedCpAsync>(p, smem, B, total, r, &kmap, &vmap);
                 goto producer_done;
             }
         }

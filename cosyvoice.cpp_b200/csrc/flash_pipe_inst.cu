@@ -12,7 +12,8 @@ namespace fp {
 template <int KT, int VT>
 static cudaError_t run(cudaStream_t s, const Params& p, const CUtensorMap& km, const CUtensorMap& vm, dim3 grid) {
     auto fn = flash_pipe_kernel<KT, VT>;
-    constexpr int smem = smem_bytes(KT, VT);
+    int smem = smem_bytes(KT, VT);
+    if (p.staged == kStagedChunk && kRawOff + 2 * p.raw_bytes > smem) smem = kRawOff + 2 * p.raw_bytes;
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     fn<<<grid, kThreads, smem, s>>>(p, km, vm);

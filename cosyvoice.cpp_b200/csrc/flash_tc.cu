@@ -123,17 +123,29 @@ cudaError_t launch_flash(cudaStream_t stream, const cvattn_flash_params& a, int*
             return cudaErrorInvalidValue;
     }
     // block-quantized K and V with 4-byte aligned rows go through the staged producer
-    // (coalesced cp.async of the raw rows, conversion in shared memory)
-    p.staged = fp::is_block_quant(a.k.type) && fp::is_block_quant(a.v.type) &&
-               ((reinterpret_cast<uintptr_t>(a.k.data) | reinterpret_cast<uintptr_t>(a.v.data)) & 3) == 0 &&
-               ((a.k.nb1 | a.k.nb2 | a.v.nb1 | a.v.nb2) & 3) == 0;
-    // its TMA form: 16-byte aligned bases and strides (the box x coordinate is the
-    // 16-byte boundary below the head's row) and rows at least one box wide
-    if (p.staged && aligned && a.n_kv > 0 && !(a.flags & CVATTN_FLASH_ONE_TILE)) {
+    // (raw rows into shared memory, conversion there); default form: coalesced cp.async
+    const bool staged = fp::is_block_quant(a.k.type) && fp::is_block_quant(a.v.type) &&
+                        ((reinterpret_cast<uintptr_t>(a.k.data) | reinterpret_cast<uintptr_t>(a.v.data)) & 3) == 0 &&
+                        ((a.k.nb1 | a.k.nb2 | a.v.nb1 | a.v.nb2) & 3) == 0;
+    p.staged = staged ? fp::kStagedCpAsync : 0;
+    if (staged && a.n_kv > 0 && !(a.flags & CVATTN_FLASH_ONE_TILE)) {
+        const long k_row = (long)a.k.n_heads * p.k_head_bytes, v_row = (long)a.v.n_heads * p.v_head_bytes;
         const int bk = fp::raw_box_bytes(a.k.type), bv = fp::raw_box_bytes(a.v.type);
-        if ((long)a.k.n_heads * p.k_head_bytes >= bk && (long)a.v.n_heads * p.v_head_bytes >= bv &&
-            make_raw_map(&km, a.k, a.n_kv, a.batch, bk) && make_raw_map(&vm, a.v, a.n_kv, a.batch, bv))
-            p.staged = 2;
+        const long chunk_k = (64 * k_row + 127) / 128 * 128, chunk_v = (64 * v_row + 127) / 128 * 128;
+        if (aligned && k_row >= bk && v_row >= bv && make_raw_map(&km, a.k, a.n_kv, a.batch, bk) &&
+            make_raw_map(&vm, a.v, a.n_kv, a.batch, bv)) {
+            // TMA boxes: 16-byte aligned bases and strides (the box x coordinate is the
+            // 16-byte boundary below the head's row), rows at least one box wide
+            p.staged = fp::kStagedBoxes;
+        } else if (((reinterpret_cast<uintptr_t>(a.k.data) | reinterpret_cast<uintptr_t>(a.v.data)) & 15) == 0 &&
+                   (a.batch == 1 || ((a.k.nb2 | a.v.nb2) & 15) == 0) && (long)a.k.nb1 == k_row &&
+                   (long)a.v.nb1 == v_row && chunk_k + chunk_v <= fp::kChunkRawMax) {
+            // bulk copies of whole rows: contiguous rows, 16-byte aligned tile starts
+            // (64 rows of a multiple of 4 bytes are a multiple of 256 bytes)
+            p.staged = fp::kStagedChunk;
+            p.raw_k_bytes = (int)chunk_k;
+            p.raw_bytes = (int)(chunk_k + chunk_v);
+        }
     }
     if (!(a.flags & CVATTN_FLASH_ONE_TILE)) {
         // persistent kernel: one CTA per SM over the query-tile pairs

@@ -70,7 +70,8 @@ struct Params {
     int bounds[CVATTN_MAX_CHUNK_BOUNDS];
     int key_offset, row_offset;
     int use_tma;
-    int staged;  // block-quantized K and V: the staged producer (flash_pipe); 2 = its TMA form
+    int staged;  // block-quantized K and V: the staged producer's copy form (flash_pipe), 0 = none
+    int raw_bytes, raw_k_bytes;  // its chunk form: raw buffer bytes and the K part (whole rows of 64 keys)
     int* status;
 };
 

@@ -248,3 +248,23 @@ def test_staged_tma_form_type_pairs(ctx, cv, cuda, oracle, kname, vname):
     q = rng.standard_normal((B, n_q, Hq, D)).astype(np.float32)
     out = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, n_kv).cpu().numpy()
     check(out, reference(oracle, kt, vt, kq, vq, q, n_kv, Hkv), f"{kname}/{vname}")
+
+
+@pytest.mark.parametrize("kname", QUANT)
+@pytest.mark.parametrize("vname", QUANT)
+def test_staged_chunk_form_type_pairs(ctx, cv, cuda, oracle, kname, vname):
+    """Qwen2's 2 KV heads: q8_0 / q4_0 / q5_0 rows (136 / 72 / 88 bytes) are not
+    16-byte multiples but are contiguous, so the producer bulk-copies a tile's
+    whole rows; 201 keys leave a 9-row last tile whose byte count is 8 past a
+    16-byte multiple (the tail goes by 4-byte copies).  Pairs of 16-byte rows
+    (q4_1, q5_1) take the TMA boxes."""
+    torch = cuda
+    kt, vt = cv.TYPE_BY_NAME[kname], cv.TYPE_BY_NAME[vname]
+    rng = np.random.default_rng(kt * 13 + vt + 9)
+    B, Hq, Hkv, n_q, n_kv = 2, 14, 2, 150, 201
+    kq, kb, kd = make_kv(cv, cuda, oracle, kt, n_kv, Hkv, B, rng, cap=n_kv + 5)
+    vq, vb, vd = make_kv(cv, cuda, oracle, vt, n_kv, Hkv, B, rng, cap=n_kv + 5)
+    q = rng.standard_normal((B, n_q, Hq, D)).astype(np.float32)
+    mask = oracle.mask_bits_to_f32(oracle.causal_mask(n_q, n_kv))[None]
+    out = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, n_kv, mask_mode=cv.MASK_CAUSAL).cpu().numpy()
+    check(out, reference(oracle, kt, vt, kq, vq, q, n_kv, Hkv, mask), f"{kname}/{vname}")
