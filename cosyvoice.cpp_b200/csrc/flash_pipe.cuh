@@ -41,9 +41,24 @@ using fa::Params;
 
 constexpr int kBN = 64;  // keys per tile
 constexpr int kStages = 6;
-constexpr int kThreads = 448;
-constexpr int kProdWarp0 = 8;
-constexpr int kMmaWarp = 12;  // warps 12 and 13: MMA issuer of query tile 0 / 1
+// The kernel's shape for H softmax warpgroups per query tile (1 or 2).  With 2,
+// warps w and w + 4 of a query tile share TMEM lane quarter w and take 32 of the
+// tile's 64 key columns each: twice the independent softmax chains per
+// sub-partition, at the cost of one exchange per tile between the two halves of
+// a row.  It pays where items are short (DiT: ~12 key tiles per query tile, with
+// Q loads and epilogues between them) and costs ~5% on long causal prefill.
+template <int H>
+struct Shape {
+    static_assert(H == 1 || H == 2, "one or two softmax warpgroups per query tile");
+    static constexpr int kSoftWarps = 8 * H;      // softmax warps of both query tiles
+    static constexpr int kSoftThreads = 128 * H;  // softmax threads of one query tile
+    static constexpr int kChunks = kBN / 32 / H;  // 32-column chunks of a tile per softmax thread
+    static constexpr int kProdWarp0 = kSoftWarps;
+    static constexpr int kMmaWarp = kSoftWarps + 4;  // MMA issuer of query tile 0 / 1
+    static constexpr int kThreads = (kMmaWarp + 2) * 32;
+};
+// Launches with n_kv up to this many keys split the softmax columns (H = 2) by default.
+constexpr int kSplitMaxKeys = 1024;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSCol = 0, kPCol = 256, kOCol = 384;  // S: x*128 + b*64, P: 256 + x*64 + b*32, O: 384 + x*64
 constexpr float kRescaleThreshold = 8.0f;
@@ -60,7 +75,9 @@ constexpr int kQOff = 0;                             // 2 x 16 KB
 constexpr int kKOff = 32 * 1024;                     // kStages x 8 KB
 constexpr int kVOff = kKOff + kStages * kTileBytes;  // kStages x 8 KB
 constexpr int kBarOff = kVOff + kStages * kTileBytes;  // 128 KB
-constexpr int kSmemBytes = kBarOff + 512;            // one CTA per SM (TMEM: 512 columns)
+constexpr int kXchOff = kBarOff + 512;               // row statistics the two column halves exchange
+constexpr int kXchBytes = 2048 * 4;
+constexpr int kSmemBytes = kXchOff + kXchBytes;      // one CTA per SM (TMEM: 512 columns)
 constexpr int kRawOff = kSmemBytes;                  // staged producer: raw rows of two tiles
 
 __host__ __device__ constexpr bool is_block_quant(int t) {
@@ -214,11 +231,11 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
     return make_float2(__int_as_float(__float_as_int(q.x) + (n0 << 23)), __int_as_float(__float_as_int(q.y) + (n1 << 23)));
 }
 
-// Row max of one S tile (64 TMEM columns), 4 independent chains.
-template <class Score>
-__device__ __forceinline__ void max_pass(uint32_t s_taddr, bool full, int jt, const Score& score, float& mt) {
+// Row max of this thread's kChunks x 32 columns of an S tile (key j0 onward), 4 independent chains.
+template <int kChunks, class Score>
+__device__ __forceinline__ void max_pass(uint32_t s_taddr, bool full, int j0, const Score& score, float& mt) {
     float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-    for (int c = 0; c < kBN / 32; ++c) {
+    for (int c = 0; c < kChunks; ++c) {
         uint32_t sv[32];
         tc::tmem_ld32(s_taddr + 32 * c, sv);
         tc::tmem_ld_wait();
@@ -227,7 +244,7 @@ __device__ __forceinline__ void max_pass(uint32_t s_taddr, bool full, int jt, co
             for (int e = 0; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], __uint_as_float(sv[e]));
         } else {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], score(sv[e], jt * kBN + 32 * c + e));
+            for (int e = 0; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], score(sv[e], j0 + 32 * c + e));
         }
     }
     mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
@@ -250,17 +267,17 @@ __device__ __forceinline__ void exp_chunk(const float (&sc)[32], float mu, __hal
     }
 }
 
-// P = 2^(s - mu) of one S tile into the tile's TMEM P columns, with the tile's
-// row sum and the largest P of the row (as f16; +inf when P overflowed f16).
+// P = 2^(s - mu) of this thread's columns of one S tile into the tile's TMEM P
+// columns, with their row sum and their largest P (as f16; +inf when P overflowed f16).
 // Full tiles (no masked entry in any row) skip the mask.  (Double-buffering
 // the four TMEM loads measured slower: the larger unrolled body costs more
 // than the load latency it hides.)
-template <class Score>
-__device__ __forceinline__ void exp_pass(uint32_t s_taddr, uint32_t p_taddr, bool full, float mu, int jt,
+template <int kChunks, class Score>
+__device__ __forceinline__ void exp_pass(uint32_t s_taddr, uint32_t p_taddr, bool full, float mu, int j0,
                                          const Score& score, float& pm, float& lt) {
     __half2 pmax = __float2half2_rn(0.0f);
     float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
-    for (int c = 0; c < kBN / 32; ++c) {
+    for (int c = 0; c < kChunks; ++c) {
         uint32_t sv[32];
         tc::tmem_ld32(s_taddr + 32 * c, sv);
         tc::tmem_ld_wait();
@@ -272,7 +289,7 @@ __device__ __forceinline__ void exp_pass(uint32_t s_taddr, uint32_t p_taddr, boo
             exp_chunk<kExpPoly>(sc, mu, pmax, acc, pw);
         } else {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) sc[e] = score(sv[e], jt * kBN + 32 * c + e);
+            for (int e = 0; e < 32; ++e) sc[e] = score(sv[e], j0 + 32 * c + e);
             exp_chunk<false>(sc, mu, pmax, acc, pw);
         }
         tc::tmem_st16(p_taddr + 16 * c, pw);
@@ -350,7 +367,7 @@ constexpr int kStagedCpAsync = 1;  // 4-byte cp.async of each head row by all 12
 constexpr int kStagedBoxes = 2;    // rows 16-byte aligned: TMA byte boxes around the head's row
 constexpr int kStagedChunk = 3;    // contiguous rows: one bulk copy of the tile's whole rows
 // Largest raw tile of the chunk form (whole K and V rows of 64 keys).
-constexpr int kChunkRawMax = 48 * 1024;
+constexpr int kChunkRawMax = 44 * 1024;
 
 // The producer role for block-quantized K and V (128 threads, r = 0..127).
 // Tiles are produced in the order the MMA issuers consume them, one raw tile
@@ -502,10 +519,12 @@ __device__ __forceinline__ void produce_staged(const Params& p, uint8_t* smem, B
     if constexpr (!kBoxes) cp_async_wait<0>();  // no copy into shared memory outlives the CTA
 }
 
-template <int KT, int VT>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int KT, int VT, int H>
+__global__ void __launch_bounds__(Shape<H>::kThreads, 1)
     flash_pipe_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap) {
+    constexpr int kHalves = H, kSoftWarps = Shape<H>::kSoftWarps, kSoftThreads = Shape<H>::kSoftThreads;
+    constexpr int kChunks = Shape<H>::kChunks, kProdWarp0 = Shape<H>::kProdWarp0, kMmaWarp = Shape<H>::kMmaWarp;
     extern __shared__ __align__(1024) uint8_t smem[];
     Bars* B = reinterpret_cast<Bars*>(smem + kBarOff);
     if (smem_addr(smem) & 1023u) {
@@ -521,12 +540,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&B->kv_empty[s], 2);  // one arrival per MMA issuer
         }
         for (int x = 0; x < 2; ++x) {
-            mbar_init(&B->q_full[x], 128);
-            mbar_init(&B->o_free[x], 128);
+            mbar_init(&B->q_full[x], kSoftThreads);
+            mbar_init(&B->o_free[x], kSoftThreads);
             mbar_init(&B->raw_full[x], 1);
             for (int b = 0; b < 2; ++b) {
                 mbar_init(&B->s_full[x][b], 1);
-                mbar_init(&B->p_ready[x][b], 128);
+                mbar_init(&B->p_ready[x][b], kSoftThreads);
                 mbar_init(&B->o_done[x][b], 1);
             }
         }
@@ -542,15 +561,40 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::fence_after();
     const uint32_t tmem = B->tmem_base;
 
-    if (warp < 8) {
-        // ====================================================== softmax group x
-        const int x = warp >> 2;
-        const int r = tid & 127;  // query row in the tile = TMEM lane
-        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-        const uint32_t s_tbase = tmem + lane_base + kSCol + x * 128;  // + buffer * 64
-        const uint32_t p_tbase = tmem + lane_base + kPCol + x * 64;   // + buffer * 32
-        const uint32_t o_taddr = tmem + lane_base + kOCol + x * 64;
+    if (warp < kSoftWarps) {
+        // ====================================================== softmax of query tile x
+        // warp = x * 4 * kHalves + hf * 4 + quad: rows quad * 32 .. + 31 (the warp's TMEM
+        // lane quarter), key columns hf * 32 * kChunks .. + 32 * kChunks - 1 of each tile
+        const int x = warp / (4 * kHalves);
+        const int hf = (warp >> 2) & (kHalves - 1);
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;  // query row in the tile = TMEM lane
+        const int col0 = hf * 32 * kChunks;
+        const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+        const uint32_t s_tbase = tmem + lane_base + kSCol + x * 128 + col0;   // + buffer * 64
+        const uint32_t p_tbase = tmem + lane_base + kPCol + x * 64 + col0 / 2;  // + buffer * 32
+        const uint32_t o_taddr = tmem + lane_base + kOCol + x * 64 + col0;    // O columns = output dims
         uint8_t* qtile = smem + kQOff + x * 16384;
+        // Row statistics the two halves of a row exchange (kHalves == 2): the largest P of a
+        // tile (by tile parity), the tile max and the row sum, each [half][row].  Every
+        // exchange is one bar.red.and over the row's two warps, which also ANDs their `ok`,
+        // so both leave together; consecutive exchanges never share a slot.
+        float* xch = reinterpret_cast<float*>(smem + kXchOff);
+        float* x_pm = xch + x * 512;          // [parity][half][128]
+        float* x_mt = xch + 1024 + x * 256;   // [half][128]
+        float* x_l = xch + 1536 + x * 256;    // [half][128]
+        const int bar_pair = 2 + x * 4 + quad;
+        auto exchange = [&](float* slots, float v, bool ok_in, float& other) -> bool {
+            if constexpr (kHalves == 2) {
+                slots[hf * 128 + r] = v;
+                const bool all = prod_bar_and(bar_pair, 64, ok_in);
+                other = slots[(hf ^ 1) * 128 + r];
+                return all;
+            } else {
+                other = v;
+                return ok_in;
+            }
+        };
         uint32_t T = 0;  // tiles of this group so far (all items): tile T uses buffer T & 1
         bool ok = true;
         for (int idx = blockIdx.x; ok && idx < total; idx += gridDim.x) {
@@ -562,27 +606,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int h = x ? it.h[1] : it.h[0], b = it.b;
             const int i0 = qt * BM, i = i0 + r;
             const bool row_ok = i < p.n_q;
+            float* orow = p.out + (((int64_t)b * p.n_q + i) * p.Hq + h) * D + col0;
             if (nt == 0) {  // no visible key for any row of the tile: zero output
                 if (row_ok) {
-                    float* orow = p.out + (((int64_t)b * p.n_q + i) * p.Hq + h) * D;
 #pragma unroll
-                    for (int c = 0; c < 16; ++c) *reinterpret_cast<float4*>(orow + 4 * c) = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int c = 0; c < 16 / kHalves; ++c)
+                        *reinterpret_cast<float4*>(orow + 4 * c) = make_float4(0.f, 0.f, 0.f, 0.f);
                 }
                 continue;
             }
-            {   // Q row -> f16 (scaled into log2 units) swizzled; the previous item's S MMAs are done
-                const float* qrow = p.q + (int64_t)b * p.q_nb_batch + (int64_t)i * p.q_nb_tok + (int64_t)h * p.q_nb_head;
-                uint32_t w[32];
+            {   // this thread's dims of the Q row -> f16 (scaled into log2 units) swizzled; the
+                // previous item's S MMAs are done
+                const float* qrow = p.q + (int64_t)b * p.q_nb_batch + (int64_t)i * p.q_nb_tok + (int64_t)h * p.q_nb_head + col0;
+                uint32_t w[32 / kHalves];
 #pragma unroll
-                for (int c = 0; c < 16; ++c) {
+                for (int c = 0; c < 16 / kHalves; ++c) {
                     const float4 v = row_ok ? *reinterpret_cast<const float4*>(qrow + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
                     const float sc = p.scale_log2;
                     w[2 * c] = tc::pack_f16x2(v.x * sc, v.y * sc);
                     w[2 * c + 1] = tc::pack_f16x2(v.z * sc, v.w * sc);
                 }
 #pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    *reinterpret_cast<uint4*>(qtile + tc::sw128_offset(r, c)) =
+                for (int c = 0; c < 8 / kHalves; ++c)
+                    *reinterpret_cast<uint4*>(qtile + tc::sw128_offset(r, col0 / 8 + c)) =
                         make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
                 fence_proxy_async_smem();
                 mbar_arrive(&B->q_full[x]);
@@ -605,36 +651,38 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int be0 = fa::block_end(p, i0 + p.row_offset);
                 full_below = min(full_below, be0 == 0x7fffffff ? p.n_kv : p.key_offset + be0);
             } else if (p.mask_mode == CVATTN_MASK_EXPLICIT) full_below = 0;
-            float m_ref = -INFINITY, l = 0.0f;
+            float m_ref = -INFINITY, l = 0.0f;  // the same m_ref in both halves of a row
             for (int jt = 0; jt < nt; ++jt, ++T) {
                 const int buf = T & 1;
                 const uint32_t s_taddr = s_tbase + buf * 64, p_taddr = p_tbase + buf * 32;
-                if (!__all_sync(0xffffffffu, wait_or_err(&B->s_full[x][buf], (T >> 1) & 1, &B->err, p.status, 1))) {
+                const int j0 = jt * kBN + col0;
+                ok = __all_sync(0xffffffffu, wait_or_err(&B->s_full[x][buf], (T >> 1) & 1, &B->err, p.status, 1));
+                if (ok) tc::fence_after();
+                if (ok && T >= 2) {  // P buffer `buf` is free once O(T-2) has read it
+                    ok = __all_sync(0xffffffffu, wait_or_err(&B->o_done[x][buf], ((T - 2) >> 1) & 1, &B->err, p.status, 2));
+                    if (ok) tc::fence_after();
+                }
+                const bool full = (jt + 1) * kBN <= full_below;
+                // One pass against the running reference max: P = 2^(s - m_ref), its row sum and
+                // its largest value.  Only when a row's P exceeds 2^threshold in either half (its max
+                // rose by more than the threshold; also a row's first visible tile) is the tile redone
+                // against the tile's own max.
+                float pm = INFINITY;
+                float lt = 0.0f;
+                if (ok && __any_sync(0xffffffffu, m_ref != -INFINITY))
+                    exp_pass<kChunks>(s_taddr, p_taddr, full, m_ref == -INFINITY ? 0.0f : m_ref, j0, score, pm, lt);
+                float pm_other;
+                if (!exchange(x_pm + (T & 1) * 256, pm, ok, pm_other)) {
                     ok = false;
                     break;
                 }
-                tc::fence_after();
-                const bool full = (jt + 1) * kBN <= full_below;
-                if (T >= 2) {  // P buffer `buf` is free once O(T-2) has read it
-                    if (!__all_sync(0xffffffffu, wait_or_err(&B->o_done[x][buf], ((T - 2) >> 1) & 1, &B->err, p.status, 2))) {
-                        ok = false;
-                        break;
-                    }
-                    tc::fence_after();
-                }
-                // One pass against the running reference max: P = 2^(s - m_ref), its row sum and
-                // its largest value.  Only when a row's P exceeds 2^threshold (its max rose by more
-                // than the threshold; also a row's first visible tile) is the tile redone against
-                // the tile's own max.
-                float pm = INFINITY;
-                float lt = 0.0f;
-                if (__any_sync(0xffffffffu, m_ref != -INFINITY))
-                    exp_pass(s_taddr, p_taddr, full, m_ref == -INFINITY ? 0.0f : m_ref, jt, score, pm, lt);
-                const bool redo = m_ref == -INFINITY || !(pm <= kRescaleP);
-                if (__any_sync(0xffffffffu, redo)) {
+                const bool redo = m_ref == -INFINITY || !(fmaxf(pm, pm_other) <= kRescaleP);
+                if (__any_sync(0xffffffffu, redo)) {  // the same vote in both halves: same rows, same m_ref
                     tc::tmem_st_wait();  // the optimistic P stores land before they are overwritten
-                    float mt = -INFINITY;
-                    max_pass(s_taddr, full, jt, score, mt);
+                    float mt = -INFINITY, mt_other;
+                    max_pass<kChunks>(s_taddr, full, j0, score, mt);
+                    exchange(x_mt, mt, true, mt_other);
+                    mt = fmaxf(mt, mt_other);
                     float alpha = 1.0f;
                     if (mt > m_ref + kRescaleThreshold) {
                         alpha = (m_ref == -INFINITY) ? 0.0f : fast_exp2(m_ref - mt);
@@ -643,12 +691,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     if (jt > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
                         // O(T-1) (the other P buffer) accumulates with the old reference first
-                        if (!__all_sync(0xffffffffu, wait_or_err(&B->o_done[x][buf ^ 1], ((T - 1) >> 1) & 1, &B->err, p.status, 11))) {
+                        bool w_ok = __all_sync(0xffffffffu, wait_or_err(&B->o_done[x][buf ^ 1], ((T - 1) >> 1) & 1, &B->err, p.status, 11));
+                        if constexpr (kHalves == 2) w_ok = prod_bar_and(bar_pair, 64, w_ok);  // both halves agree
+                        if (!w_ok) {
                             ok = false;
                             break;
                         }
                         tc::fence_after();
-                        for (int c = 0; c < 2; ++c) {
+                        for (int c = 0; c < kChunks; ++c) {  // this thread's O columns
                             uint32_t ov[32];
                             tc::tmem_ld32(o_taddr + 32 * c, ov);
                             tc::tmem_ld_wait();
@@ -658,7 +708,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                     lt = 0.0f;
-                    exp_pass(s_taddr, p_taddr, full, m_ref == -INFINITY ? 0.0f : m_ref, jt, score, pm, lt);
+                    exp_pass<kChunks>(s_taddr, p_taddr, full, m_ref == -INFINITY ? 0.0f : m_ref, j0, score, pm, lt);
                 }
                 l += lt;
                 tc::tmem_st_wait();
@@ -666,14 +716,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive(&B->p_ready[x][buf]);
             }
             if (!ok) break;
-            // epilogue: O_x of the item's last tile (T - 1) complete
-            if (!__all_sync(0xffffffffu, wait_or_err(&B->o_done[x][(T - 1) & 1], ((T - 1) >> 1) & 1, &B->err, p.status, 3))) {
+            // epilogue: O_x of the item's last tile (T - 1) complete; the row sum of both halves
+            ok = __all_sync(0xffffffffu, wait_or_err(&B->o_done[x][(T - 1) & 1], ((T - 1) >> 1) & 1, &B->err, p.status, 3));
+            float l_other;
+            if (!exchange(x_l, l, ok, l_other)) {
                 ok = false;
                 break;
             }
+            if constexpr (kHalves == 2) l += l_other;
             tc::fence_after();
-            float o[64];
-            for (int c = 0; c < 2; ++c) {
+            float o[64 / kHalves];
+            for (int c = 0; c < kChunks; ++c) {
                 uint32_t ov[32];
                 tc::tmem_ld32(o_taddr + 32 * c, ov);
                 tc::tmem_ld_wait();
@@ -684,9 +737,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive(&B->o_free[x]);
             if (row_ok) {
                 const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-                float* orow = p.out + (((int64_t)b * p.n_q + i) * p.Hq + h) * D;
 #pragma unroll
-                for (int c = 0; c < 16; ++c)
+                for (int c = 0; c < 16 / kHalves; ++c)
                     *reinterpret_cast<float4*>(orow + 4 * c) =
                         make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv, o[4 * c + 3] * inv);
             }

@@ -9,15 +9,20 @@
 namespace cvattn {
 namespace fp {
 
-template <int KT, int VT>
-static cudaError_t run(cudaStream_t s, const Params& p, const CUtensorMap& km, const CUtensorMap& vm, dim3 grid) {
-    auto fn = flash_pipe_kernel<KT, VT>;
+template <int KT, int VT, int H>
+static cudaError_t run_h(cudaStream_t s, const Params& p, const CUtensorMap& km, const CUtensorMap& vm, dim3 grid) {
+    auto fn = flash_pipe_kernel<KT, VT, H>;
     int smem = smem_bytes(KT, VT);
     if (p.staged == kStagedChunk && kRawOff + 2 * p.raw_bytes > smem) smem = kRawOff + 2 * p.raw_bytes;
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    fn<<<grid, kThreads, smem, s>>>(p, km, vm);
+    fn<<<grid, Shape<H>::kThreads, smem, s>>>(p, km, vm);
     return cudaGetLastError();
+}
+
+template <int KT, int VT>
+static cudaError_t run(cudaStream_t s, const Params& p, const CUtensorMap& km, const CUtensorMap& vm, dim3 grid) {
+    return p.halves == 2 ? run_h<KT, VT, 2>(s, p, km, vm, grid) : run_h<KT, VT, 1>(s, p, km, vm, grid);
 }
 
 template <>

@@ -72,6 +72,7 @@ struct Params {
     int use_tma;
     int staged;  // block-quantized K and V: the staged producer's copy form (flash_pipe), 0 = none
     int raw_bytes, raw_k_bytes;  // its chunk form: raw buffer bytes and the K part (whole rows of 64 keys)
+    int halves;  // persistent kernel: softmax warpgroups per query tile (1 or 2)
     int* status;
 };
 

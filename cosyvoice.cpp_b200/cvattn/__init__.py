@@ -34,6 +34,8 @@ DECODE_WIDE_CHUNKS = 16
 DECODE_TMEM_STREAM = 32
 DECODE_WARP_MMA = 64
 FLASH_ONE_TILE = 1
+FLASH_SPLIT_COLUMNS = 2
+FLASH_WHOLE_ROWS = 4
 ROPE_NORMAL, ROPE_NEOX = 0, 2
 
 OK = 0
@@ -277,7 +279,9 @@ def flash_params(q, k: Tensor, v: Tensor, n_kv: int, out, mask_mode: int = MASK_
                  causal_offset: int | None = None, chunk_bounds: Sequence[int] = (), chunk_key_offset: int = 0,
                  chunk_row_offset: int = 0, scale: float | None = None, flags: int = 0) -> FlashParams:
     """q f32 [batch, n_q, Hq, D] (any strides, D contiguous); out f32 [batch, n_q, Hq, D] contiguous.
-    flags: FLASH_ONE_TILE selects the one-query-tile-per-CTA kernel instead of the persistent one."""
+    flags: FLASH_ONE_TILE selects the one-query-tile-per-CTA kernel instead of the persistent one;
+    FLASH_SPLIT_COLUMNS / FLASH_WHOLE_ROWS force the persistent kernel's softmax shape (two
+    warpgroups per query tile, each on half the key columns / one, a thread per row)."""
     B, n_q, Hq, D = q.shape
     p = FlashParams()
     p.q = q.data_ptr()

@@ -340,7 +340,13 @@ typedef struct cvattn_flash_params {
 enum {
     /* one query tile per CTA, shared-memory P (the first tensor-core kernel);
        the default is the persistent two-tile kernel with P in tensor memory */
-    CVATTN_FLASH_ONE_TILE = 1
+    CVATTN_FLASH_ONE_TILE = 1,
+    /* persistent kernel: two softmax warpgroups per query tile, each taking half
+       of every key tile's columns (the default for n_kv <= 1024) */
+    CVATTN_FLASH_SPLIT_COLUMNS = 2,
+    /* persistent kernel: one softmax warpgroup per query tile, a thread per row
+       (the default for n_kv > 1024) */
+    CVATTN_FLASH_WHOLE_ROWS = 4
 };
 
 cvattn_status cvattn_flash(cvattn_context* ctx, void* stream, const cvattn_flash_params* p);

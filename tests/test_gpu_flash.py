@@ -43,10 +43,12 @@ def reference(oracle, t_k, t_v, kq, vq, q, n_kv, Hkv, mask=None):
     return out
 
 
-@pytest.fixture(params=["pipelined", "one_tile"])
+@pytest.fixture(params=["split_columns", "whole_rows", "one_tile"])
 def fk(request, cv):
-    """flags of cvattn_flash: the persistent two-tile kernel (default) or the one-tile kernel."""
-    return 0 if request.param == "pipelined" else cv.FLASH_ONE_TILE
+    """flags of cvattn_flash: the persistent two-tile kernel with two softmax warpgroups per
+    query tile (each on half the key columns) or one (a thread per row), or the one-tile kernel."""
+    return {"split_columns": cv.FLASH_SPLIT_COLUMNS, "whole_rows": cv.FLASH_WHOLE_ROWS,
+            "one_tile": cv.FLASH_ONE_TILE}[request.param]
 
 
 def check(out, ref, what=""):
