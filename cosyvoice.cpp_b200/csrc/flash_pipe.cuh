@@ -322,6 +322,17 @@ __device__ __forceinline__ bool prod_bar_and(int id, int n, bool v) {
     return r != 0;
 }
 
+// Number of the n threads at barrier `id` whose v is true (bar.red.popc).
+__device__ __forceinline__ int prod_bar_count(int id, int n, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.popc.u32 %0, %2, %3, p;\n\t}"
+        : "=r"(r) : "r"((uint32_t)v), "r"(id), "r"(n) : "memory");
+    return (int)r;
+}
+
 __device__ __forceinline__ void cp_async4(void* smem_dst, const void* gmem_src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"(smem_addr(smem_dst)), "l"(gmem_src) : "memory");
 }
@@ -575,12 +586,11 @@ __global__ void __launch_bounds__(Shape<H>::kThreads, 1)
         const uint32_t p_tbase = tmem + lane_base + kPCol + x * 64 + col0 / 2;  // + buffer * 32
         const uint32_t o_taddr = tmem + lane_base + kOCol + x * 64 + col0;    // O columns = output dims
         uint8_t* qtile = smem + kQOff + x * 16384;
-        // Row statistics the two halves of a row exchange (kHalves == 2): the largest P of a
-        // tile (by tile parity), the tile max and the row sum, each [half][row].  Every
-        // exchange is one bar.red.and over the row's two warps, which also ANDs their `ok`,
-        // so both leave together; consecutive exchanges never share a slot.
+        // Row statistics the two halves of a row exchange (kHalves == 2): the tile max of a
+        // redone tile and the row sum, each [half][row].  Every exchange is one bar.red.and
+        // over the row's two warps, which also ANDs their `ok`, so both leave together;
+        // consecutive exchanges never share a slot (a vote barrier separates two tile maxima).
         float* xch = reinterpret_cast<float*>(smem + kXchOff);
-        float* x_pm = xch + x * 512;          // [parity][half][128]
         float* x_mt = xch + 1024 + x * 256;   // [half][128]
         float* x_l = xch + 1536 + x * 256;    // [half][128]
         const int bar_pair = 2 + x * 4 + quad;
@@ -671,13 +681,22 @@ __global__ void __launch_bounds__(Shape<H>::kThreads, 1)
                 float lt = 0.0f;
                 if (ok && __any_sync(0xffffffffu, m_ref != -INFINITY))
                     exp_pass<kChunks>(s_taddr, p_taddr, full, m_ref == -INFINITY ? 0.0f : m_ref, j0, score, pm, lt);
-                float pm_other;
-                if (!exchange(x_pm + (T & 1) * 256, pm, ok, pm_other)) {
-                    ok = false;
+                bool redo = m_ref == -INFINITY || !(pm <= kRescaleP);
+                if constexpr (kHalves == 2) {
+                    // one vote over the row's two warps: nothing to do (the common case), or some
+                    // thread failed a wait or needs the tile redone -- then both halves redo every
+                    // row (rows whose max did not rise keep their reference max, alpha = 1)
+                    if (prod_bar_count(bar_pair, 64, !ok || redo) != 0) {
+                        if (!prod_bar_and(bar_pair, 64, ok)) {
+                            ok = false;
+                            break;
+                        }
+                        redo = true;
+                    }
+                } else if (!ok) {
                     break;
                 }
-                const bool redo = m_ref == -INFINITY || !(fmaxf(pm, pm_other) <= kRescaleP);
-                if (__any_sync(0xffffffffu, redo)) {  // the same vote in both halves: same rows, same m_ref
+                if (__any_sync(0xffffffffu, redo)) {  // the same decision in both halves of a row
                     tc::tmem_st_wait();  // the optimistic P stores land before they are overwritten
                     float mt = -INFINITY, mt_other;
                     max_pass<kChunks>(s_taddr, full, j0, score, mt);
