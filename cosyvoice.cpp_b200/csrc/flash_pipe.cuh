@@ -41,12 +41,13 @@ using fa::Params;
 
 constexpr int kBN = 64;  // keys per tile
 constexpr int kStages = 6;
-// The kernel's shape for H softmax warpgroups per query tile (1 or 2).  With 2,
-// warps w and w + 4 of a query tile share TMEM lane quarter w and take 32 of the
-// tile's 64 key columns each: twice the independent softmax chains per
-// sub-partition, at the cost of one exchange per tile between the two halves of
-// a row.  It pays where items are short (DiT: ~12 key tiles per query tile, with
-// Q loads and epilogues between them) and costs ~5% on long causal prefill.
+// The kernel's shape for H softmax warpgroups per query tile (1 or 2).  With 2
+// (the default), warps w and w + 4 of a query tile share TMEM lane quarter w and
+// take 32 of the tile's 64 key columns each: twice the independent softmax
+// chains per sub-partition, at the cost of one vote per tile between the two
+// halves of a row.  It pays where items are short (DiT: ~12 key tiles per query
+// tile, with Q loads and epilogues between them) and breaks even on long
+// causal prefill.
 template <int H>
 struct Shape {
     static_assert(H == 1 || H == 2, "one or two softmax warpgroups per query tile");
@@ -57,8 +58,6 @@ struct Shape {
     static constexpr int kMmaWarp = kSoftWarps + 4;  // MMA issuer of query tile 0 / 1
     static constexpr int kThreads = (kMmaWarp + 2) * 32;
 };
-// Launches with n_kv up to this many keys split the softmax columns (H = 2) by default.
-constexpr int kSplitMaxKeys = 1024;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSCol = 0, kPCol = 256, kOCol = 384;  // S: x*128 + b*64, P: 256 + x*64 + b*32, O: 384 + x*64
 constexpr float kRescaleThreshold = 8.0f;

@@ -149,10 +149,8 @@ cudaError_t launch_flash(cudaStream_t stream, const cvattn_flash_params& a, int*
     }
     if (!(a.flags & CVATTN_FLASH_ONE_TILE)) {
         // persistent kernel: one CTA per SM over the query-tile pairs; the softmax columns
-        // split over two warpgroups per query tile for short key ranges unless a flag says
-        p.halves = (a.flags & CVATTN_FLASH_WHOLE_ROWS)       ? 1
-                   : (a.flags & CVATTN_FLASH_SPLIT_COLUMNS) ? 2
-                   : (a.n_kv <= fp::kSplitMaxKeys ? 2 : 1);
+        // split over two warpgroups per query tile unless CVATTN_FLASH_WHOLE_ROWS
+        p.halves = (a.flags & CVATTN_FLASH_WHOLE_ROWS) ? 1 : 2;
         const int num_sms = current_sm_count();
         if (num_sms <= 0) return cudaErrorInvalidDevice;
         // the item count of fp::n_items: head pairs for an even G, query-tile pairs otherwise

@@ -342,10 +342,9 @@ enum {
        the default is the persistent two-tile kernel with P in tensor memory */
     CVATTN_FLASH_ONE_TILE = 1,
     /* persistent kernel: two softmax warpgroups per query tile, each taking half
-       of every key tile's columns (the default for n_kv <= 1024) */
+       of every key tile's columns (the default) */
     CVATTN_FLASH_SPLIT_COLUMNS = 2,
-    /* persistent kernel: one softmax warpgroup per query tile, a thread per row
-       (the default for n_kv > 1024) */
+    /* persistent kernel: one softmax warpgroup per query tile, a thread per row */
     CVATTN_FLASH_WHOLE_ROWS = 4
 };
 
