@@ -230,20 +230,56 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
     return make_float2(__int_as_float(__float_as_int(q.x) + (n0 << 23)), __int_as_float(__float_as_int(q.y) + (n1 << 23)));
 }
 
+// The mask of one softmax row.  The causal and chunk masks (and n_kv) are a
+// prefix of the keys: key j is visible iff j < lim (causal: j <= causal_offset
+// + i, src/cosyvoice-llm.cpp:20-29; chunk: j < key_offset or j - key_offset <
+// the row's block end, src/cosyvoice-token2wav.cpp:285-298, i.e. j <
+// key_offset + block end).  An explicit f16 mask adds mrow[j] (times log2 e)
+// to the visible keys j < lim = n_kv.  A chunk of 32 columns whose keys all lie
+// below wlim, the smallest lim of the warp's 32 rows, needs no mask (a
+// warp-uniform test).
+struct RowMask {
+    int lim;
+    int wlim;
+    bool explicit_mask;     // uniform over the CTA
+    const uint16_t* mrow;   // explicit mask row (read only below lim)
+};
+
+// Scores of the 32 columns of a chunk whose first key is jc: log2 units, -inf
+// past the row's limit (plus the explicit mask).
+__device__ __forceinline__ void mask_chunk(const uint32_t (&sv)[32], int jc, const RowMask& rm, float (&sc)[32]) {
+    const int rem = rm.lim - jc;  // columns e < rem are visible
+    if (rm.explicit_mask) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+            sc[e] = e < rem ? __uint_as_float(sv[e]) + h2f(rm.mrow[jc + e]) * 1.4426950408889634f : -INFINITY;
+    } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) sc[e] = e < rem ? __uint_as_float(sv[e]) : -INFINITY;
+    }
+}
+
+__device__ __forceinline__ bool chunk_unmasked(int jc, const RowMask& rm) {
+    return !rm.explicit_mask && jc + 32 <= rm.wlim;
+}
+
 // Row max of this thread's kChunks x 32 columns of an S tile (key j0 onward), 4 independent chains.
-template <int kChunks, class Score>
-__device__ __forceinline__ void max_pass(uint32_t s_taddr, bool full, int j0, const Score& score, float& mt) {
+template <int kChunks>
+__device__ __forceinline__ void max_pass(uint32_t s_taddr, int j0, const RowMask& rm, float& mt) {
     float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
     for (int c = 0; c < kChunks; ++c) {
         uint32_t sv[32];
         tc::tmem_ld32(s_taddr + 32 * c, sv);
         tc::tmem_ld_wait();
-        if (full) {
+        const int jc = j0 + 32 * c;
+        if (chunk_unmasked(jc, rm)) {
 #pragma unroll
             for (int e = 0; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], __uint_as_float(sv[e]));
         } else {
+            float sc[32];
+            mask_chunk(sv, jc, rm, sc);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], score(sv[e], j0 + 32 * c + e));
+            for (int e = 0; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], sc[e]);
         }
     }
     mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
@@ -268,12 +304,12 @@ __device__ __forceinline__ void exp_chunk(const float (&sc)[32], float mu, __hal
 
 // P = 2^(s - mu) of this thread's columns of one S tile into the tile's TMEM P
 // columns, with their row sum and their largest P (as f16; +inf when P overflowed f16).
-// Full tiles (no masked entry in any row) skip the mask.  (Double-buffering
+// Chunks with no masked entry in the warp's rows skip the mask.  (Double-buffering
 // the four TMEM loads measured slower: the larger unrolled body costs more
 // than the load latency it hides.)
-template <int kChunks, class Score>
-__device__ __forceinline__ void exp_pass(uint32_t s_taddr, uint32_t p_taddr, bool full, float mu, int j0,
-                                         const Score& score, float& pm, float& lt) {
+template <int kChunks>
+__device__ __forceinline__ void exp_pass(uint32_t s_taddr, uint32_t p_taddr, float mu, int j0, const RowMask& rm,
+                                         float& pm, float& lt) {
     __half2 pmax = __float2half2_rn(0.0f);
     float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
     for (int c = 0; c < kChunks; ++c) {
@@ -282,13 +318,13 @@ __device__ __forceinline__ void exp_pass(uint32_t s_taddr, uint32_t p_taddr, boo
         tc::tmem_ld_wait();
         float sc[32];
         uint32_t pw[16];
-        if (full) {
+        const int jc = j0 + 32 * c;
+        if (chunk_unmasked(jc, rm)) {
 #pragma unroll
             for (int e = 0; e < 32; ++e) sc[e] = __uint_as_float(sv[e]);
             exp_chunk<kExpPoly>(sc, mu, pmax, acc, pw);
         } else {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) sc[e] = score(sv[e], j0 + 32 * c + e);
+            mask_chunk(sv, jc, rm, sc);
             exp_chunk<false>(sc, mu, pmax, acc, pw);
         }
         tc::tmem_st16(p_taddr + 16 * c, pw);
@@ -642,24 +678,23 @@ __global__ void __launch_bounds__(Shape<H>::kThreads, 1)
                 fence_proxy_async_smem();
                 mbar_arrive(&B->q_full[x]);
             }
-            const int be = (p.mask_mode == CVATTN_MASK_CHUNK) ? fa::block_end(p, i + p.row_offset) : 0;
-            const uint16_t* mrow = (p.mask_mode == CVATTN_MASK_EXPLICIT && row_ok)
-                                       ? p.mask + (int64_t)b * p.mask_nb2 + (int64_t)i * p.mask_nb1
-                                       : nullptr;
-            auto score = [&](uint32_t bits, int j) -> float {
-                float s = __uint_as_float(bits);
-                bool vis = j < p.n_kv && row_ok;
-                if (p.mask_mode == CVATTN_MASK_CAUSAL) vis = vis && (j <= p.causal_offset + i);
-                else if (p.mask_mode == CVATTN_MASK_CHUNK) vis = vis && (j < p.key_offset || j - p.key_offset < be);
-                else if (p.mask_mode == CVATTN_MASK_EXPLICIT && vis) s += h2f(mrow[j]) * 1.4426950408889634f;
-                return vis ? s : -INFINITY;
-            };
-            int full_below = p.n_kv;  // first key at which some row of the tile may be masked
-            if (p.mask_mode == CVATTN_MASK_CAUSAL) full_below = min(full_below, p.causal_offset + i0 + 1);
-            else if (p.mask_mode == CVATTN_MASK_CHUNK) {
-                const int be0 = fa::block_end(p, i0 + p.row_offset);
-                full_below = min(full_below, be0 == 0x7fffffff ? p.n_kv : p.key_offset + be0);
-            } else if (p.mask_mode == CVATTN_MASK_EXPLICIT) full_below = 0;
+            RowMask rm;
+            {
+                rm.explicit_mask = p.mask_mode == CVATTN_MASK_EXPLICIT;
+                rm.mrow = (rm.explicit_mask && row_ok) ? p.mask + (int64_t)b * p.mask_nb2 + (int64_t)i * p.mask_nb1
+                                                      : p.mask;
+                int lim = p.n_kv;
+                if (p.mask_mode == CVATTN_MASK_CAUSAL) {
+                    lim = min(lim, p.causal_offset + i + 1);
+                } else if (p.mask_mode == CVATTN_MASK_CHUNK) {
+                    const int be = fa::block_end(p, i + p.row_offset);
+                    if (be != 0x7fffffff) lim = min(lim, p.key_offset + max(be, 0));
+                }
+                // A row past n_q is never written out: its scores (zero Q) stay unmasked so the
+                // warp's other rows keep the unmasked path (with an explicit mask: nothing visible).
+                rm.lim = row_ok ? lim : (rm.explicit_mask ? 0 : 0x7fffffff);
+                rm.wlim = __reduce_min_sync(0xffffffffu, rm.lim);
+            }
             float m_ref = -INFINITY, l = 0.0f;  // the same m_ref in both halves of a row
             for (int jt = 0; jt < nt; ++jt, ++T) {
                 const int buf = T & 1;
@@ -671,7 +706,6 @@ __global__ void __launch_bounds__(Shape<H>::kThreads, 1)
                     ok = __all_sync(0xffffffffu, wait_or_err(&B->o_done[x][buf], ((T - 2) >> 1) & 1, &B->err, p.status, 2));
                     if (ok) tc::fence_after();
                 }
-                const bool full = (jt + 1) * kBN <= full_below;
                 // One pass against the running reference max: P = 2^(s - m_ref), its row sum and
                 // its largest value.  Only when a row's P exceeds 2^threshold in either half (its max
                 // rose by more than the threshold; also a row's first visible tile) is the tile redone
@@ -679,7 +713,7 @@ __global__ void __launch_bounds__(Shape<H>::kThreads, 1)
                 float pm = INFINITY;
                 float lt = 0.0f;
                 if (ok && __any_sync(0xffffffffu, m_ref != -INFINITY))
-                    exp_pass<kChunks>(s_taddr, p_taddr, full, m_ref == -INFINITY ? 0.0f : m_ref, j0, score, pm, lt);
+                    exp_pass<kChunks>(s_taddr, p_taddr, m_ref == -INFINITY ? 0.0f : m_ref, j0, rm, pm, lt);
                 bool redo = m_ref == -INFINITY || !(pm <= kRescaleP);
                 if constexpr (kHalves == 2) {
                     // one vote over the row's two warps: nothing to do (the common case), or some
@@ -698,7 +732,7 @@ __global__ void __launch_bounds__(Shape<H>::kThreads, 1)
                 if (__any_sync(0xffffffffu, redo)) {  // the same decision in both halves of a row
                     tc::tmem_st_wait();  // the optimistic P stores land before they are overwritten
                     float mt = -INFINITY, mt_other;
-                    max_pass<kChunks>(s_taddr, full, j0, score, mt);
+                    max_pass<kChunks>(s_taddr, j0, rm, mt);
                     exchange(x_mt, mt, true, mt_other);
                     mt = fmaxf(mt, mt_other);
                     float alpha = 1.0f;
@@ -726,7 +760,7 @@ __global__ void __launch_bounds__(Shape<H>::kThreads, 1)
                         }
                     }
                     lt = 0.0f;
-                    exp_pass<kChunks>(s_taddr, p_taddr, full, m_ref == -INFINITY ? 0.0f : m_ref, j0, score, pm, lt);
+                    exp_pass<kChunks>(s_taddr, p_taddr, m_ref == -INFINITY ? 0.0f : m_ref, j0, rm, pm, lt);
                 }
                 l += lt;
                 tc::tmem_st_wait();
