@@ -61,7 +61,12 @@ struct Shape {
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSCol = 0, kPCol = 256, kOCol = 384;  // S: x*128 + b*64, P: 256 + x*64 + b*32, O: 384 + x*64
 constexpr float kRescaleThreshold = 8.0f;
-constexpr float kRescaleP = 256.0f;  // 2^kRescaleThreshold
+// The optimistic pass of a tile is redone against the tile's own max when a thread's sum of P
+// over its columns exceeds kRedoSum (some P > 2^7: the row's max rose by more than 7 since
+// the reference was set); without a redo every P <= kRedoSum, far inside f16.  (Starting
+// the prefix masks' rows from the reference max 0, so that the first tile needs no redo,
+// measured slower: causal prefill 462 -> 444 TFLOP/s, DiT 292 -> 289.)
+constexpr float kRedoSum = 4096.0f;
 #ifndef CVATTN_FLASH_EXP_POLY
 #define CVATTN_FLASH_EXP_POLY 0
 #endif
@@ -236,11 +241,13 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
 // the row's block end, src/cosyvoice-token2wav.cpp:285-298, i.e. j <
 // key_offset + block end).  An explicit f16 mask adds mrow[j] (times log2 e)
 // to the visible keys j < lim = n_kv.  A chunk of 32 columns whose keys all lie
-// below wlim, the smallest lim of the warp's 32 rows, needs no mask (a
-// warp-uniform test).
+// below wlim, the smallest lim of the warp's 32 rows, needs no mask, and one
+// that starts at or past wmax, the largest, has no visible entry (warp-uniform
+// tests).
 struct RowMask {
     int lim;
     int wlim;
+    int wmax;               // the largest lim of the warp's rows: chunks at or past it are fully masked
     bool explicit_mask;     // uniform over the CTA
     const uint16_t* mrow;   // explicit mask row (read only below lim)
 };
@@ -268,10 +275,11 @@ template <int kChunks>
 __device__ __forceinline__ void max_pass(uint32_t s_taddr, int j0, const RowMask& rm, float& mt) {
     float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
     for (int c = 0; c < kChunks; ++c) {
+        const int jc = j0 + 32 * c;
+        if (jc >= rm.wmax) continue;  // no visible entry in the warp's rows (warp-uniform)
         uint32_t sv[32];
         tc::tmem_ld32(s_taddr + 32 * c, sv);
         tc::tmem_ld_wait();
-        const int jc = j0 + 32 * c;
         if (chunk_unmasked(jc, rm)) {
 #pragma unroll
             for (int e = 0; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], __uint_as_float(sv[e]));
@@ -286,11 +294,9 @@ __device__ __forceinline__ void max_pass(uint32_t s_taddr, int j0, const RowMask
 }
 
 // P = 2^(s - mu) of 32 scores (f16 pairs into pw), with the running sum (two
-// chains) and the running f16 max of P (two elementwise maxima per instruction).
-// kPoly: one pair in four is exponentiated on the FMA pipe.
+// chains).  kPoly: one pair in four is exponentiated on the FMA pipe.
 template <bool kPoly>
-__device__ __forceinline__ void exp_chunk(const float (&sc)[32], float mu, __half2& pmax, float2 (&acc)[2],
-                                          uint32_t (&pw)[16]) {
+__device__ __forceinline__ void exp_chunk(const float (&sc)[32], float mu, float2 (&acc)[2], uint32_t (&pw)[16]) {
     const float2 neg_mu = make_float2(-mu, -mu), one = make_float2(1.0f, 1.0f);
 #pragma unroll
     for (int e = 0; e < 32; e += 2) {
@@ -298,39 +304,40 @@ __device__ __forceinline__ void exp_chunk(const float (&sc)[32], float mu, __hal
         const float2 pp = (kPoly && ((e >> 1) & 3) == 3) ? exp2_poly2(xx) : make_float2(fast_exp2(xx.x), fast_exp2(xx.y));
         acc[(e >> 1) & 1] = ffma2(pp, one, acc[(e >> 1) & 1]);
         pw[e / 2] = tc::pack_f16x2(pp.x, pp.y);
-        pmax = __hmax2(pmax, *reinterpret_cast<const __half2*>(&pw[e / 2]));
     }
 }
 
 // P = 2^(s - mu) of this thread's columns of one S tile into the tile's TMEM P
-// columns, with their row sum and their largest P (as f16; +inf when P overflowed f16).
-// Chunks with no masked entry in the warp's rows skip the mask.  (Double-buffering
-// the four TMEM loads measured slower: the larger unrolled body costs more
-// than the load latency it hides.)
+// columns; returns their sum.  Chunks with no masked entry in the warp's rows skip
+// the mask; chunks with no visible entry in the warp's rows write zeros without
+// reading S.  (Double-buffering the four TMEM loads measured slower: the larger
+// unrolled body costs more than the load latency it hides.)
 template <int kChunks>
-__device__ __forceinline__ void exp_pass(uint32_t s_taddr, uint32_t p_taddr, float mu, int j0, const RowMask& rm,
-                                         float& pm, float& lt) {
-    __half2 pmax = __float2half2_rn(0.0f);
+__device__ __forceinline__ float exp_pass(uint32_t s_taddr, uint32_t p_taddr, float mu, int j0, const RowMask& rm) {
     float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
     for (int c = 0; c < kChunks; ++c) {
-        uint32_t sv[32];
-        tc::tmem_ld32(s_taddr + 32 * c, sv);
-        tc::tmem_ld_wait();
-        float sc[32];
         uint32_t pw[16];
         const int jc = j0 + 32 * c;
-        if (chunk_unmasked(jc, rm)) {
+        if (jc >= rm.wmax) {  // warp-uniform
 #pragma unroll
-            for (int e = 0; e < 32; ++e) sc[e] = __uint_as_float(sv[e]);
-            exp_chunk<kExpPoly>(sc, mu, pmax, acc, pw);
+            for (int i = 0; i < 16; ++i) pw[i] = 0u;
         } else {
-            mask_chunk(sv, jc, rm, sc);
-            exp_chunk<false>(sc, mu, pmax, acc, pw);
+            uint32_t sv[32];
+            tc::tmem_ld32(s_taddr + 32 * c, sv);
+            tc::tmem_ld_wait();
+            float sc[32];
+            if (chunk_unmasked(jc, rm)) {
+#pragma unroll
+                for (int e = 0; e < 32; ++e) sc[e] = __uint_as_float(sv[e]);
+                exp_chunk<kExpPoly>(sc, mu, acc, pw);
+            } else {
+                mask_chunk(sv, jc, rm, sc);
+                exp_chunk<false>(sc, mu, acc, pw);
+            }
         }
         tc::tmem_st16(p_taddr + 16 * c, pw);
     }
-    pm = fmaxf(__low2float(pmax), __high2float(pmax));
-    lt = (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y);
+    return (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y);
 }
 
 
@@ -694,6 +701,7 @@ __global__ void __launch_bounds__(Shape<H>::kThreads, 1)
                 // warp's other rows keep the unmasked path (with an explicit mask: nothing visible).
                 rm.lim = row_ok ? lim : (rm.explicit_mask ? 0 : 0x7fffffff);
                 rm.wlim = __reduce_min_sync(0xffffffffu, rm.lim);
+                rm.wmax = __reduce_max_sync(0xffffffffu, rm.lim);
             }
             float m_ref = -INFINITY, l = 0.0f;  // the same m_ref in both halves of a row
             for (int jt = 0; jt < nt; ++jt, ++T) {
@@ -706,15 +714,13 @@ __global__ void __launch_bounds__(Shape<H>::kThreads, 1)
                     ok = __all_sync(0xffffffffu, wait_or_err(&B->o_done[x][buf], ((T - 2) >> 1) & 1, &B->err, p.status, 2));
                     if (ok) tc::fence_after();
                 }
-                // One pass against the running reference max: P = 2^(s - m_ref), its row sum and
-                // its largest value.  Only when a row's P exceeds 2^threshold in either half (its max
-                // rose by more than the threshold; also a row's first visible tile) is the tile redone
-                // against the tile's own max.
-                float pm = INFINITY;
+                // One pass against the running reference max: P = 2^(s - m_ref) and its sum.  Only
+                // when a thread's sum exceeds kRedoSum (the row's max rose), and on a row's first
+                // visible tile, is the tile redone against the tile's own max.
                 float lt = 0.0f;
                 if (ok && __any_sync(0xffffffffu, m_ref != -INFINITY))
-                    exp_pass<kChunks>(s_taddr, p_taddr, m_ref == -INFINITY ? 0.0f : m_ref, j0, rm, pm, lt);
-                bool redo = m_ref == -INFINITY || !(pm <= kRescaleP);
+                    lt = exp_pass<kChunks>(s_taddr, p_taddr, m_ref == -INFINITY ? 0.0f : m_ref, j0, rm);
+                bool redo = m_ref == -INFINITY || !(lt <= kRedoSum);
                 if constexpr (kHalves == 2) {
                     // one vote over the row's two warps: nothing to do (the common case), or some
                     // thread failed a wait or needs the tile redone -- then both halves redo every
@@ -759,8 +765,7 @@ __global__ void __launch_bounds__(Shape<H>::kThreads, 1)
                             tc::tmem_st32(o_taddr + 32 * c, ov);
                         }
                     }
-                    lt = 0.0f;
-                    exp_pass<kChunks>(s_taddr, p_taddr, m_ref == -INFINITY ? 0.0f : m_ref, j0, rm, pm, lt);
+                    lt = exp_pass<kChunks>(s_taddr, p_taddr, m_ref == -INFINITY ? 0.0f : m_ref, j0, rm);
                 }
                 l += lt;
                 tc::tmem_st_wait();

@@ -270,3 +270,56 @@ def test_staged_chunk_form_type_pairs(ctx, cv, cuda, oracle, kname, vname):
     mask = oracle.mask_bits_to_f32(oracle.causal_mask(n_q, n_kv))[None]
     out = cv.flash(ctx, torch.tensor(q, device="cuda"), kd, vd, n_kv, mask_mode=cv.MASK_CAUSAL).cpu().numpy()
     check(out, reference(oracle, kt, vt, kq, vq, q, n_kv, Hkv, mask), f"{kname}/{vname}")
+
+
+@pytest.mark.parametrize("mode", ["large", "tiny", "negative", "growing"])
+@pytest.mark.parametrize("kv_name", ["f16", "q8_0"])
+@pytest.mark.parametrize("mask_name", ["none", "causal", "chunk"])
+@pytest.mark.parametrize("Hq,Hkv", [(14, 2), (4, 4)])
+def test_flash_score_ranges(ctx, cv, cuda, oracle, fk, mode, kv_name, mask_name, Hq, Hkv):
+    """Score magnitudes that exercise the softmax's reference-max logic: large scores
+    (the first tile's reference max 0 overflows and is redone), scores near 0, scores far
+    below 0 (the first tile's P underflows and is redone), and scores that grow along the
+    keys (repeated rescales of O)."""
+    torch = cuda
+    t = cv.TYPE_BY_NAME[kv_name]
+    rng = np.random.default_rng(11 * Hq + len(mode) + 3 * len(mask_name))
+    B, n_q, n_kv = 1, 200, 300
+    u = np.full(D, 1.0 / 8.0, np.float32)  # |u| = 1
+    kx = rng.standard_normal((B, n_kv, Hkv * D)).astype(np.float32)
+    qx = rng.standard_normal((B, n_q, Hq, D)).astype(np.float32)
+    if mode == "large":
+        qx *= 10.0
+    elif mode == "tiny":
+        qx *= 1e-3
+    elif mode == "negative":  # q.k ~ -180 for every key: scores near -32 in log2 units
+        kx += 3.0 * np.tile(u, Hkv)[None, None]
+        qx = 0.1 * qx - 60.0 * u[None, None, None]
+    else:  # growing: q.k rises from ~0 to ~300 along the keys
+        ramp = (np.arange(n_kv, dtype=np.float32) / n_kv * 30.0)[None, :, None]
+        kx += ramp * np.tile(u, Hkv)[None, None]
+        qx = 0.3 * qx + 10.0 * u[None, None, None]
+    kq = oracle.quantize(t, kx)
+    kd = cv.kv_tensor(torch.tensor(kq.reshape(-1), device="cuda"), t, Hkv, D, n_kv, B)
+    vq, vb, vd = make_kv(cv, cuda, oracle, t, n_kv, Hkv, B, rng)
+    kw, mask = {}, None
+    if mask_name == "causal":
+        kw = {"mask_mode": cv.MASK_CAUSAL}
+        mask = oracle.mask_bits_to_f32(oracle.causal_mask(n_q, n_kv))[None]
+    elif mask_name == "chunk":
+        bounds = list(range(40, n_q + 1, 40))
+        kw = {"mask_mode": cv.MASK_CHUNK, "chunk_bounds": bounds, "chunk_key_offset": n_kv - n_q}
+        cm = oracle.mask_bits_to_f32(oracle.chunk_mask(n_q, bounds))
+        mask = np.concatenate([np.zeros((n_q, n_kv - n_q), np.float32), cm], axis=1)[None]
+    out = cv.flash(ctx, torch.tensor(qx, device="cuda"), kd, vd, n_kv, flags=fk, **kw).cpu().numpy()
+    # At scores of tens of log2 units the f16 rounding of Q (and of K) alone moves the output by
+    # more than the f16 bar's max-abs (a float64 model of f16 operands gives 9.5e-3 for "large"),
+    # so the reference takes the operands as the kernel rounds them: Q * scale * log2(e) in f32
+    # rounded to f16, K and V dequantized and rounded to f16.  What remains is the softmax logic
+    # under test (P in f16, fp32 accumulation).
+    sl2 = np.float32(0.125 * 1.4426950408889634)
+    q16 = (qx * sl2).astype(np.float16).astype(np.float64) / float(sl2)
+    kr = oracle.dequantize(t, kq[0, :n_kv], Hkv * D).astype(np.float16).astype(np.float32).reshape(n_kv, Hkv, D)
+    vr = oracle.dequantize(t, vq[0, :n_kv], Hkv * D).astype(np.float16).astype(np.float32).reshape(n_kv, Hkv, D)
+    ref = oracle.attention_f64(q16[0].astype(np.float32), kr, vr, 1.0 / 8.0, None if mask is None else mask[0])[None]
+    check(out, ref, f"{mode} {kv_name} {mask_name} {Hq}/{Hkv}")
