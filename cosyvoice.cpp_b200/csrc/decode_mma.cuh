@@ -37,6 +37,8 @@
 // KV head) elects the last writer, which merges the runs listed from the cut.
 #pragma once
 
+#include <type_traits>
+
 #include "decode_stream.cuh"
 
 namespace cvattn {
@@ -53,19 +55,27 @@ constexpr int kMaxThreads = 64 * kMaxPairs;
 constexpr int kMaxSeq = 512;    // prefix table in shared memory
 constexpr float kLazyLog2 = 8.0f;
 constexpr int kEvMin = -3, kEvMax = 6;
+constexpr int kSmemLimit = 227 * 1024;  // dynamic shared memory of one CTA
 
 __host__ __device__ constexpr int rup(int x, int a) { return (x + a - 1) / a * a; }
 
 // Shared memory: prefix table, lengths, barriers (full / empty per pair and
-// slot), error flag, then the raw rings of the pairs.
+// slot), error flag, the per-warp scale tables of the current item, then the raw
+// rings of the pairs.  A warp's scale table holds, per position pair q (positions
+// 2q, 2q + 1 of the item), float4s {x[2q][blk 0], x[2q+1][blk 0], x[2q][blk 1],
+// x[2q+1][blk 1]} of: the K scale, the V scale times 2^ev (the P' factor), and,
+// for types with a min, the centred K and V mins.
 struct Smem {
-    int pref, slen, bars, misc, ring0, stage, vofs, pair_stride, total;
-    __host__ __device__ Smem(int rowK, int rowV, int pairs) {
+    int pref, slen, bars, misc, scl, scl_warp, ring0, stage, vofs, pair_stride, total;
+    __host__ __device__ Smem(int rowK, int rowV, int pairs, bool k_min, bool v_min) {
         int o = 0;
         pref = o;  o += rup((kMaxSeq + 1) * 4, 16);
         slen = o;  o += kMaxSeq * 4;
         bars = o;  o += rup(kMaxPairs * kStages * 2 * 8, 16);
         misc = o;  o += 16;
+        scl = o;
+        scl_warp = 32 * 16 * (2 + (k_min ? 1 : 0) + (v_min ? 1 : 0));
+        o += 2 * pairs * scl_warp;
         o = rup(o, 128);
         ring0 = o;
         vofs = kC * rowK;                       // V rows follow the K rows of a slot
@@ -348,7 +358,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
     constexpr int GBK = group_bytes(KT), GBV = group_bytes(VT);
     constexpr int headK = 2 * GBK, headV = 2 * GBV, rowK = 2 * headK, rowV = 2 * headV;
     constexpr bool K_MIN = BlockTraits<KT>::HAS_MIN, V_MIN = BlockTraits<VT>::HAS_MIN;
-    const Smem L(rowK, rowV, n_pairs);
+    const Smem L(rowK, rowV, n_pairs, K_MIN, V_MIN);
     const bool emit_partial = (a.flags & CVATTN_DECODE_EMIT_PARTIAL) != 0;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
     volatile int* err = reinterpret_cast<volatile int*>(smem + L.misc);
@@ -421,6 +431,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
     const int lo = (int)(gp * n_items / P);
     const int n_local = (int)((gp + 1) * n_items / P) - lo;
     uint8_t* ring = smem + L.ring0 + pair * L.pair_stride;
+    float4* sK = reinterpret_cast<float4*>(smem + L.scl + warp * L.scl_warp);  // this warp's scale table
+    float4* sV = sK + 32;
+    float4* sKm = sV + 32;                  // K mins (types with a min)
+    float4* sVm = sKm + (K_MIN ? 32 : 0);   // V mins (types with a min)
     uint64_t* pbars = bars + pair * kStages * 2;
     const bool producer = g == 0 && lane == 0;
 
@@ -555,16 +569,32 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
             fence_proxy_async_smem();  // the slot is later overwritten by the bulk copies
             __syncwarp();
         }
-        // V exponent of each block for this run: max |d_V| over the item's positions
+        // Scale table of the item (this warp's KV head): lane q converts the block scales
+        // (and mins) of positions 2q and 2q + 1 once, for the four lanes that read them in
+        // the sub-steps below.  Positions past n get zero V weight (P' = 0, no min term),
+        // so only the scores of a partial item need a mask.  The V exponent of each block
+        // for this run comes from max |d_V| over the item's positions.
         int evn[2];
         {
+            float dk[2][2], dvv[2][2], mk[2][2], mvv[2][2];  // [position of the pair][block]
             float vm[2] = {0.0f, 0.0f};
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
-                const int pos = lane + 32 * u;
-                if (pos < n) {
+                const int pos = 2 * lane + u;
+                const bool valid = pos < n;
 #pragma unroll
-                    for (int b = 0; b < 2; ++b) vm[b] = fmaxf(vm[b], fabsf(h2f((uint16_t)ld_u16(Vst + pos * rowV + b * GBV))));
+                for (int b = 0; b < 2; ++b) {
+                    dk[u][b] = mk[u][b] = dvv[u][b] = mvv[u][b] = 0.0f;
+                    if (valid) {
+                        const uint8_t* kr = Kst + pos * rowK + b * GBK;
+                        dk[u][b] = h2f((uint16_t)ld_u16(kr));
+                        if constexpr (K_MIN) {
+                            constexpr float kCentre = BlockTraits<KT>::OFF_QH >= 0 ? 16.0f : 8.0f;
+                            mk[u][b] = fmaf(kCentre, dk[u][b], h2f((uint16_t)ld_u16(kr + BlockTraits<KT>::OFF_M)));
+                        }
+                        vscale<VT>(Vst + pos * rowV + b * GBV, dvv[u][b], mvv[u][b]);
+                        vm[b] = fmaxf(vm[b], fabsf(dvv[u][b]));
+                    }
                 }
             }
 #pragma unroll
@@ -577,6 +607,12 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
                     evn[b] = (x < kEvMin || x > kEvMax) ? dstream::v_exp_target(vm[b]) : ev[b];
                 }
             }
+            const float f0 = pow2f(evn[0]), f1 = pow2f(evn[1]);
+            sK[lane] = make_float4(dk[0][0], dk[1][0], dk[0][1], dk[1][1]);
+            sV[lane] = make_float4(dvv[0][0] * f0, dvv[1][0] * f0, dvv[0][1] * f1, dvv[1][1] * f1);
+            if constexpr (K_MIN) sKm[lane] = make_float4(mk[0][0], mk[1][0], mk[0][1], mk[1][1]);
+            if constexpr (V_MIN) sVm[lane] = make_float4(mvv[0][0], mvv[1][0], mvv[0][1], mvv[1][1]);
+            __syncwarp();
         }
         if (run_n == 0) {
 #pragma unroll
@@ -600,12 +636,14 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
         }
         ev[0] = evn[0];
         ev[1] = evn[1];
-        const float fev0 = pow2f(ev[0]), fev1 = pow2f(ev[1]);
 
-#pragma unroll 1
-        for (int sub = 0; sub < kC / 16; ++sub) {
-            if (16 * sub >= n) break;
-            // ---- S = Q . K^T for two 8-position tiles, per K block
+        // One 16-position sub-step: S = Q.K^T for two 8-position tiles, the scores of head gid
+        // at this lane's 4 positions (log2 units), the lazy reference max, P' = P d_V 2^ev split
+        // into the A fragments of P.V, and O += P'.V over 8 dim tiles.  kFull: all 64 positions
+        // of the item are valid, no score needs a mask.  (Lanes of a padding head, gid >= G, run
+        // on zero Q rows: finite scores whose rows of O are never written.)
+        auto sub_step = [&](auto full_tag, int sub) {
+            constexpr bool kFull = decltype(full_tag)::value;
             float acc[2][2][4];
 #pragma unroll
             for (int b = 0; b < 2; ++b)
@@ -624,28 +662,26 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
                 mma16816(acc[1][tt], qa[1][0], r[0], r[1]);
                 mma16816(acc[1][tt], qa[1][1], r[2], r[3]);
             }
-            // ---- scores of head gid at this lane's 4 positions (log2 units)
             float sc[4];
-            int pp[4];
+            float4 dvq[2], mvq[2];
 #pragma unroll
-            for (int tt = 0; tt < 2; ++tt)
+            for (int tt = 0; tt < 2; ++tt) {
+                const int q = 8 * sub + 4 * tt + tig;  // positions 2q, 2q + 1
+                const float4 dk = sK[q];
+                dvq[tt] = sV[q];
+                float4 mk = make_float4(0.f, 0.f, 0.f, 0.f);
+                if constexpr (K_MIN) mk = sKm[q];
+                if constexpr (V_MIN) mvq[tt] = sVm[q];
 #pragma unroll
                 for (int i = 0; i < 2; ++i) {
-                    const int k = 2 * tt + i;
-                    const int pos = 16 * sub + 8 * tt + 2 * tig + i;
-                    pp[k] = pos;
-                    const uint8_t* kr = Kst + pos * rowK;
-                    const float d0 = h2f((uint16_t)ld_u16(kr)), d1 = h2f((uint16_t)ld_u16(kr + GBK));
+                    const float d0 = i ? dk.y : dk.x, d1 = i ? dk.w : dk.z;
                     float v = d0 * (acc[0][tt][i] + acc[0][tt][2 + i]) + d1 * (acc[1][tt][i] + acc[1][tt][2 + i]);
                     v *= esc;
-                    if constexpr (K_MIN) {
-                        constexpr float kCentre = BlockTraits<KT>::OFF_QH >= 0 ? 16.0f : 8.0f;
-                        const float m0 = fmaf(kCentre, d0, h2f((uint16_t)ld_u16(kr + BlockTraits<KT>::OFF_M)));
-                        const float m1 = fmaf(kCentre, d1, h2f((uint16_t)ld_u16(kr + GBK + BlockTraits<KT>::OFF_M)));
-                        v += m0 * qsum[0] + m1 * qsum[1];
-                    }
-                    sc[k] = (pos < n && head_ok) ? v : -INFINITY;
+                    if constexpr (K_MIN) v += (i ? mk.y : mk.x) * qsum[0] + (i ? mk.w : mk.z) * qsum[1];
+                    if constexpr (!kFull) v = (2 * q + i < n) ? v : -INFINITY;
+                    sc[2 * tt + i] = v;
                 }
+            }
             // ---- lazy reference max of head gid (uniform decision per warp)
             {
                 const float mx = quad_max(fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3])));
@@ -670,23 +706,23 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
             float p[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                p[k] = sc[k] == -INFINITY ? 0.0f : fast_exp2(sc[k] - mref);
-                lsum += p[k];
+                if constexpr (kFull) p[k] = fast_exp2(sc[k] - mref);
+                else p[k] = sc[k] == -INFINITY ? 0.0f : fast_exp2(sc[k] - mref);
             }
+            lsum += (p[0] + p[1]) + (p[2] + p[3]);
             uint32_t pa[2][4];
 #pragma unroll
             for (int b = 0; b < 2; ++b) {
-                float x[4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    float dv, mv;
-                    vscale<VT>(Vst + pp[k] * rowV + b * GBV, dv, mv);
-                    const bool ok = pp[k] < n;
-                    x[k] = ok ? p[k] * (dv * (b ? fev1 : fev0)) : 0.0f;
-                    if constexpr (V_MIN) pmv[b] = fmaf(ok ? p[k] : 0.0f, ok ? mv : 0.0f, pmv[b]);
+                const float x0 = p[0] * (b ? dvq[0].z : dvq[0].x), x1 = p[1] * (b ? dvq[0].w : dvq[0].y);
+                const float x2 = p[2] * (b ? dvq[1].z : dvq[1].x), x3 = p[3] * (b ? dvq[1].w : dvq[1].y);
+                if constexpr (V_MIN) {
+                    pmv[b] = fmaf(p[0], b ? mvq[0].z : mvq[0].x, pmv[b]);
+                    pmv[b] = fmaf(p[1], b ? mvq[0].w : mvq[0].y, pmv[b]);
+                    pmv[b] = fmaf(p[2], b ? mvq[1].z : mvq[1].x, pmv[b]);
+                    pmv[b] = fmaf(p[3], b ? mvq[1].w : mvq[1].y, pmv[b]);
                 }
-                split2(x[0], x[1], pa[b][0], pa[b][1]);
-                split2(x[2], x[3], pa[b][2], pa[b][3]);
+                split2(x0, x1, pa[b][0], pa[b][1]);
+                split2(x2, x3, pa[b][2], pa[b][3]);
             }
             // ---- O += P' . V, 8 dim tiles (4 per V block)
             {
@@ -701,6 +737,13 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
 #pragma unroll
                 for (int jj = 0; jj < 4; ++jj) mma16816(O[4 + jj], pa[1], v0[jj], v1[jj]);
             }
+        };
+        if (n == kC) {
+#pragma unroll 1
+            for (int sub = 0; sub < kC / 16; ++sub) sub_step(std::true_type{}, sub);
+        } else {
+#pragma unroll 1
+            for (int sub = 0; sub < kC / 16 && 16 * sub < n; ++sub) sub_step(std::false_type{}, sub);
         }
         // slot s may be refilled once both warps are done with it
         __syncwarp();
@@ -801,8 +844,9 @@ inline bool supported_type(int t) { return t == kQ4_0 || t == kQ4_1 || t == kQ5_
 // Warp pairs per CTA for this type pair: as many as fit the shared-memory budget.
 inline int max_pairs(int k_type, int v_type) {
     const int rowK = (int)type_row_bytes(k_type, 2 * kD), rowV = (int)type_row_bytes(v_type, 2 * kD);
+    const bool k_min = k_type == kQ4_1 || k_type == kQ5_1, v_min = v_type == kQ4_1 || v_type == kQ5_1;
     int p = kMaxPairs;
-    while (p > 1 && Smem(rowK, rowV, p).total > 220 * 1024) --p;
+    while (p > 1 && Smem(rowK, rowV, p, k_min, v_min).total > kSmemLimit) --p;
     return p;
 }
 

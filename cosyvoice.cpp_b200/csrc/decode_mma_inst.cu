@@ -23,7 +23,7 @@ static cudaError_t run(cudaStream_t s, const Args& a, int n_sms) {
 
     const long ctas_needed = (items + pairs - 1) / pairs;
     const int grid = (int)(ctas_needed < n_sms ? (ctas_needed > 0 ? ctas_needed : 1) : n_sms);
-    const int smem = Smem(rowK, rowV, pairs).total;
+    const int smem = Smem(rowK, rowV, pairs, BlockTraits<KT>::HAS_MIN, BlockTraits<VT>::HAS_MIN).total;
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
