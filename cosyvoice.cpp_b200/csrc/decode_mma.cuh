@@ -56,6 +56,14 @@ constexpr int kMaxSeq = 512;    // prefix table in shared memory
 constexpr float kLazyLog2 = 8.0f;
 constexpr int kEvMin = -3, kEvMax = 6;
 constexpr int kSmemLimit = 227 * 1024;  // dynamic shared memory of one CTA
+constexpr int kMaxTasks = 4 * kMaxPairs;  // merges a CTA can be elected for: two per warp
+constexpr int kMaxMergeRuns = 32;         // runs a CTA-wide merge takes (more: the warp merges alone)
+
+// A merge the CTA was elected for: the runs of (sequence seq, KV head g), whose
+// nruns workspace slots are listed at int offset `slots` of the scale tables.
+struct MergeTask {
+    int seq, g, nruns, slots;
+};
 
 __host__ __device__ constexpr int rup(int x, int a) { return (x + a - 1) / a * a; }
 
@@ -66,13 +74,14 @@ __host__ __device__ constexpr int rup(int x, int a) { return (x + a - 1) / a * a
 // x[2q+1][blk 1]} of: the K scale, the V scale times 2^ev (the P' factor), and,
 // for types with a min, the centred K and V mins.
 struct Smem {
-    int pref, slen, bars, misc, scl, scl_warp, ring0, stage, vofs, pair_stride, total;
+    int pref, slen, bars, misc, tasks, scl, scl_warp, ring0, stage, vofs, pair_stride, total;
     __host__ __device__ Smem(int rowK, int rowV, int pairs, bool k_min, bool v_min) {
         int o = 0;
         pref = o;  o += rup((kMaxSeq + 1) * 4, 16);
         slen = o;  o += kMaxSeq * 4;
         bars = o;  o += rup(kMaxPairs * kStages * 2 * 8, 16);
-        misc = o;  o += 16;
+        misc = o;  o += 16;                     // error flag, merge task count
+        tasks = o; o += kMaxTasks * 16;         // merge tasks of the CTA (MergeTask)
         scl = o;
         scl_warp = 32 * 16 * (2 + (k_min ? 1 : 0) + (v_min ? 1 : 0));
         o += 2 * pairs * scl_warp;
@@ -240,7 +249,17 @@ __device__ __forceinline__ bool lwait(uint64_t* bar, uint32_t parity, volatile i
 }
 
 // Pair holding item i under the cut of n items over P pairs.
-__device__ __forceinline__ int pair_of(long long i, long long n, long long P) { return (int)(((i + 1) * P - 1) / n); }
+__device__ __forceinline__ int pair_of(long long i, long long n, long long P) {
+    const unsigned long long x = (unsigned long long)((i + 1) * P - 1);
+    if ((x >> 32) == 0 && (n >> 32) == 0) return (int)((uint32_t)x / (uint32_t)n);  // 32-bit division
+    return (int)(x / (unsigned long long)n);
+}
+// First item of pair bb under the cut of n items over P pairs: bb n / P.
+__device__ __forceinline__ long long cut_at(long long bb, long long n, long long P) {
+    const unsigned long long x = (unsigned long long)(bb * n);
+    if ((x >> 32) == 0 && (P >> 32) == 0) return (long long)((uint32_t)x / (uint32_t)P);
+    return (long long)(x / (unsigned long long)P);
+}
 
 // Log-sum-exp merge of the runs of (sequence seq, KV head group qh0 / G) by one
 // warp: the runs are the non-empty intersections of the sequence's items with
@@ -256,7 +275,7 @@ __device__ __forceinline__ void merge_runs(const Args& a, int seq, long long ps,
     const float* seq_ml = a.ws_ml + ((int64_t)seq * a.ws_chunks) * Hq * 2;
     const float* seq_o = a.ws_o + ((int64_t)seq * a.ws_chunks) * Hq * kD;
     auto run_slot = [&](int bb, bool& valid) {
-        const long long blo = (long long)bb * n_items / P, bhi = (long long)(bb + 1) * n_items / P;
+        const long long blo = cut_at(bb, n_items, P), bhi = cut_at(bb + 1, n_items, P);
         valid = bb <= b1 && bhi > blo;  // a pair without items writes nothing
         return valid ? (int)((blo > ps ? blo : ps) - ps) : 0;
     };
@@ -372,6 +391,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
             mbar_init(&bars[2 * i + 1], 2u);  // empty: one arrive per warp of the pair
         }
         *err = 0;
+        reinterpret_cast<int*>(smem + L.misc)[1] = 0;  // merge tasks posted
         fence_mbar_init();
     }
     // With CVATTN_DECODE_INPUTS_READY the lengths and cached rows are final: the
@@ -664,6 +684,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
             }
             float sc[4];
             float4 dvq[2], mvq[2];
+            (void)mvq;
 #pragma unroll
             for (int tt = 0; tt < 2; ++tt) {
                 const int q = 8 * sub + 4 * tt + tig;  // positions 2q, 2q + 1
@@ -812,11 +833,85 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
         run_n = 0;
     }
 
+    // ---- The merges this CTA's warps were elected for (the last writer of a sequence's runs for
+    // one KV head), done by every thread of the CTA: the elected warp lists the run slots in its
+    // scale table (free after the loop) and posts a task; after one CTA barrier, thread =
+    // (task, head, 4 dims) loads up to 8 runs' (max, sum) and outputs at once, so a sequence
+    // split over many pairs costs a round or two of L2 loads instead of one warp's many.  (A
+    // sequence over more than kMaxMergeRuns pairs, and every merge of a one-pair CTA, whose two
+    // warps would otherwise share 64 threads, is merged by its warp alone.)
+    int* mcount = reinterpret_cast<int*>(smem + L.misc) + 1;
+    MergeTask* tasks = reinterpret_cast<MergeTask*>(smem + L.tasks);
+    int* slot_tab = reinterpret_cast<int*>(smem + L.scl);
     __syncwarp();  // the lanes' partial loads follow lane 0's acquire
     for (int i = 0; i < n_merge && i < 2; ++i) {
-        const int sq = i ? mseq1 : mseq0;
-        merge_runs(a, sq, pref[sq], i ? mn1 : mn0, n_items, P, qh0, lane, a.out + (int64_t)sq * a.out_seq_stride);
-        if (lane == 0) a.ws_cnt[(int64_t)sq * 2 + g] = 0u;
+        const int sq = i ? mseq1 : mseq0, nch = i ? mn1 : mn0;
+        const long long ps = pref[sq];
+        const int b0 = pair_of(ps, n_items, P), b1 = pair_of(ps + nch - 1, n_items, P);
+        if (b1 - b0 + 1 > kMaxMergeRuns || n_pairs < 2) {  // (one pair: its two warps merge in parallel)
+            merge_runs(a, sq, ps, nch, n_items, P, qh0, lane, a.out + (int64_t)sq * a.out_seq_stride);
+            if (lane == 0) a.ws_cnt[(int64_t)sq * 2 + g] = 0u;
+            continue;
+        }
+        int c = -1;  // lane r: the slot of pair b0 + r's run (none when the pair has no items)
+        if (lane <= b1 - b0) {
+            const long long blo = cut_at(b0 + lane, n_items, P), bhi = cut_at(b0 + lane + 1, n_items, P);
+            if (bhi > blo) c = (int)((blo > ps ? blo : ps) - ps);
+        }
+        const uint32_t vm = __ballot_sync(0xffffffffu, c >= 0);
+        const int off = (warp * L.scl_warp) / 4 + i * kMaxMergeRuns;
+        if (c >= 0) slot_tab[off + __popc(vm & ((1u << lane) - 1u))] = c;
+        if (lane == 0) tasks[atomicAdd(mcount, 1)] = MergeTask{sq, g, __popc(vm), off};
+    }
+    __syncthreads();  // tasks posted; the electing acquires precede every thread's partial loads
+    {
+        const int n_tasks = *mcount;
+        for (int w = tid; w < n_tasks * G * (kD / 4); w += blockDim.x) {
+            const MergeTask T = tasks[w / (G * (kD / 4))];
+            const int h = (w / (kD / 4)) % G, dq = (w % (kD / 4)) * 4;
+            const int qh = T.g * G + h, R = T.nruns;
+            const int* slots = slot_tab + T.slots;
+            const float* seq_ml = a.ws_ml + ((int64_t)T.seq * a.ws_chunks) * Hq * 2;
+            const float* seq_o = a.ws_o + ((int64_t)T.seq * a.ws_chunks) * Hq * kD;
+            float M = -INFINITY, Ls = 0.0f;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int r0 = 0; r0 < R; r0 += 8) {
+                float2 ml[8];
+                float4 v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int cc = slots[min(r0 + j, R - 1)];
+                    ml[j] = __ldcg(reinterpret_cast<const float2*>(seq_ml + ((int64_t)cc * Hq + qh) * 2));
+                    v[j] = dpipe::ldcg_f4(seq_o + ((int64_t)cc * Hq + qh) * kD + dq);
+                }
+                float bm = M;
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    if (r0 + j < R) bm = fmaxf(bm, ml[j].x);
+                const float rs = (M == -INFINITY) ? 0.0f : fast_exp2(M - bm);
+                Ls *= rs;
+                acc.x *= rs; acc.y *= rs; acc.z *= rs; acc.w *= rs;
+                M = bm;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (r0 + j >= R) break;
+                    const float wj = ml[j].x == -INFINITY ? 0.0f : fast_exp2(ml[j].x - M);
+                    Ls = fmaf(wj, ml[j].y, Ls);
+                    acc.x = fmaf(wj, v[j].x, acc.x); acc.y = fmaf(wj, v[j].y, acc.y);
+                    acc.z = fmaf(wj, v[j].z, acc.z); acc.w = fmaf(wj, v[j].w, acc.w);
+                }
+            }
+            float* out = a.out + (int64_t)T.seq * a.out_seq_stride;
+            const float inv = emit_partial ? 1.0f : 1.0f / Ls;
+            *reinterpret_cast<float4*>(out + qh * kD + dq) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+            if (dq == 0) {
+                if (emit_partial) {
+                    a.partial_ml[((int64_t)T.seq * Hq + qh) * 2] = M;
+                    a.partial_ml[((int64_t)T.seq * Hq + qh) * 2 + 1] = Ls;
+                }
+                if (h == 0) a.ws_cnt[(int64_t)T.seq * 2 + T.g] = 0u;  // the ticket is not read again in this launch
+            }
+        }
     }
 
     // copies still in flight into this pair's ring (an early exit) complete before the CTA ends

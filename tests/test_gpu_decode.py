@@ -355,3 +355,30 @@ def test_decode_running_rescales(ctx, cv, cuda, oracle, kname, vname, path):
     ref = reference(oracle, kt, vt, kq, vq, q, lens)
     for s in range(n):
         assert rel_l2(out[s], ref[s]) <= REL_L2, f"seq {s} rel-L2 {rel_l2(out[s], ref[s]):.3e}"
+
+
+@pytest.mark.parametrize("path", ["warp_mma", "tmem_stream"])
+@pytest.mark.parametrize("shape", ["one_long", "six_runs_per_cta", "headline_mix"])
+def test_decode_merge_shapes(ctx, cv, cuda, oracle, path, shape):
+    """Split sequences merged at the end of the launch: one sequence over more than 32
+    warp pairs (merged by its elected warp alone), 148 sequences of six chunks (six runs
+    of a sequence inside one CTA, several merges per CTA), and the headline's mix of 64
+    sequences with lengths in [128, 2048]."""
+    torch = cuda
+    kt, vt = cv.Q8_0, cv.Q4_0
+    rng = np.random.default_rng(53)
+    if shape == "one_long":
+        lens = [5000, 1, 64, 65, 127]
+    elif shape == "six_runs_per_cta":
+        lens = [384] * 148
+    else:
+        lens = np.random.default_rng(0).integers(128, 2049, 64).tolist()
+    cap = max(lens)
+    kq, vq, kb, vb, kd, vd = build(cv, cuda, oracle, kt, vt, lens, rng, cap=cap)
+    q = rng.standard_normal((len(lens), HQ, D)).astype(np.float32)
+    kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    for _ in range(2):  # the tickets are left at zero for the next launch
+        out = cv.decode(ctx, torch.tensor(q, device="cuda"), kd, vd, kl, cap, **PATHS[path]).cpu().numpy()
+        ref = reference(oracle, kt, vt, kq, vq, q, lens)
+        assert rel_l2(out, ref) <= REL_L2, f"rel-L2 {rel_l2(out, ref):.3e}"
+        assert np.abs(out - ref).max() <= MAX_ABS
