@@ -58,6 +58,7 @@ constexpr int kEvMin = -3, kEvMax = 6;
 constexpr int kSmemLimit = 227 * 1024;  // dynamic shared memory of one CTA
 constexpr int kMaxTasks = 4 * kMaxPairs;  // merges a CTA can be elected for: two per warp
 constexpr int kMaxMergeRuns = 32;         // runs a CTA-wide merge takes (more: the warp merges alone)
+constexpr int kMergeBatch = 16;           // runs whose (max, sum) and outputs a merging thread loads at once
 
 // A merge the CTA was elected for: the runs of (sequence seq, KV head g), whose
 // nruns workspace slots are listed at int offset `slots` of the scale tables.
@@ -836,7 +837,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
     // ---- The merges this CTA's warps were elected for (the last writer of a sequence's runs for
     // one KV head), done by every thread of the CTA: the elected warp lists the run slots in its
     // scale table (free after the loop) and posts a task; after one CTA barrier, thread =
-    // (task, head, 4 dims) loads up to 8 runs' (max, sum) and outputs at once, so a sequence
+    // (task, head, 4 dims) loads up to kMergeBatch runs' (max, sum) and outputs at once, so a sequence
     // split over many pairs costs a round or two of L2 loads instead of one warp's many.  (A
     // sequence over more than kMaxMergeRuns pairs, and every merge of a one-pair CTA, whose two
     // warps would otherwise share 64 threads, is merged by its warp alone.)
@@ -875,25 +876,25 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
             const float* seq_o = a.ws_o + ((int64_t)T.seq * a.ws_chunks) * Hq * kD;
             float M = -INFINITY, Ls = 0.0f;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int r0 = 0; r0 < R; r0 += 8) {
-                float2 ml[8];
-                float4 v[8];
+            for (int r0 = 0; r0 < R; r0 += kMergeBatch) {
+                float2 ml[kMergeBatch];
+                float4 v[kMergeBatch];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
+                for (int j = 0; j < kMergeBatch; ++j) {
                     const int cc = slots[min(r0 + j, R - 1)];
                     ml[j] = __ldcg(reinterpret_cast<const float2*>(seq_ml + ((int64_t)cc * Hq + qh) * 2));
                     v[j] = dpipe::ldcg_f4(seq_o + ((int64_t)cc * Hq + qh) * kD + dq);
                 }
                 float bm = M;
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
+                for (int j = 0; j < kMergeBatch; ++j)
                     if (r0 + j < R) bm = fmaxf(bm, ml[j].x);
                 const float rs = (M == -INFINITY) ? 0.0f : fast_exp2(M - bm);
                 Ls *= rs;
                 acc.x *= rs; acc.y *= rs; acc.z *= rs; acc.w *= rs;
                 M = bm;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
+                for (int j = 0; j < kMergeBatch; ++j) {
                     if (r0 + j >= R) break;
                     const float wj = ml[j].x == -INFINITY ? 0.0f : fast_exp2(ml[j].x - M);
                     Ls = fmaf(wj, ml[j].y, Ls);
