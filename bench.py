@@ -324,7 +324,10 @@ def run_ours(args, rank: int, world: int, torch, dist) -> dict | None:
         "tok_per_s": round(world * N_SEQ / (ms_per_step * 1e-3), 1),
         "frac_hbm_peak": round(value / world / peaks["hbm_gbs"], 4),
         "e2e": e2e,
-        "roofline": {"bound": "hbm", "kernel": "decode_stream_kernel<q8_0,q8_0>", "achieved": round(achieved, 1),
+        "roofline": {"bound": "hbm",
+                     "kernel": decode_kernel_name(N_SEQ, N_SEQ * (CAP // 64),
+                                                  torch.cuda.get_device_properties(dev).multi_processor_count)
+                     + "<q8_0,q8_0>", "achieved": round(achieved, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                      "peak_source": peaks["source"], "launch_us": round(launch_us, 3),
                      "algorithmic_bytes_per_launch": bytes_per_layer, "traffic": traffic},
@@ -528,6 +531,22 @@ def build_cfg4(torch, cv, ctx, kt: int, vt: int, gen, n: int = 256, L: int = 409
     return dec, (kb, vb, kd, vd, q, out, kl)
 
 
+def decode_kernel_name(n_seq: int, items: int, n_sms: int, max_pairs: int = 6) -> str:
+    """The persistent decode kernel the dispatcher picks for n_seq block-quantized sequences and
+    `items` 64-position items (the rule of dmma::mma_pays / launch_shape in
+    csrc/decode_mma.cuh, for type pairs that fit six warp pairs per CTA)."""
+    if items >= 32 * n_sms:
+        return "decode_mma_kernel"
+    if n_seq <= 0 or items < 2 * n_sms:
+        return "decode_stream_kernel"
+    per_sm = -(-items // n_sms)
+    pairs = min(max_pairs, max(per_sm, 1))
+    if per_sm <= 16:
+        pairs = min(pairs, 4)
+    grid = min(n_sms, max(-(-items // pairs), 1))
+    return "decode_mma_kernel" if grid * pairs // n_seq + 1 <= 32 else "decode_stream_kernel"
+
+
 def run_decode_cfg4_sharded(torch, cv, ctx, rank: int, world: int, dist, reps: int = 10) -> dict:
     """256 sequences x 4096 positions, (q8_0, q4_0) and (q5_1, q5_1), K/V with
     1% outliers at +-8 sigma, sharded by sequence over the ranks (shard_by_length;
@@ -554,9 +573,8 @@ def run_decode_cfg4_sharded(torch, cv, ctx, rank: int, world: int, dist, reps: i
         gbs = nbytes_total / (ms * 1e-3) / 1e9
         achieved = nbytes_rank / (ms_rank * 1e-3) / 1e9
         key = "decode_cfg4_" + name.replace("/", "_")
-        # the dispatcher's rule (csrc/decode.cu): at least 32 64-position items per SM -> warp-MMA kernel
         n_sms = torch.cuda.get_device_properties(0).multi_processor_count
-        kname = "decode_mma_kernel" if mine * (L // 64) >= 32 * n_sms else "decode_stream_kernel"
+        kname = decode_kernel_name(mine, mine * (L // 64), n_sms)
         res[key] = {
             "what": f"decode 256 seqs x 4096, {name}, one layer, sequences sharded over {world} GPU(s)",
             "gbs": round(gbs, 1), "us_per_launch": round(ms * 1000.0, 2), "seqs_per_gpu": mine,

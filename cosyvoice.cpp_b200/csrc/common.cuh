@@ -117,17 +117,23 @@ __device__ __forceinline__ void store_u16(uint8_t* p, uint16_t v) {
     *reinterpret_cast<uint16_t*>(p) = v;
 }
 
-// Quantize element x (lane j of a warp) of one block into dst[0, BYTES).
-// Every lane must call it (warp-collective).
+// Quantize element x (lane j of a warp) of one block into dst[0, BYTES) and, when
+// dst2 is not null, the same bytes into dst2 (one computation, two stores).
+// Every lane must call it (warp-collective); dst2 is the same on every lane.
 template <int T>
-__device__ __forceinline__ void quantize_block_warp(float x, uint8_t* dst, int lane) {
+__device__ __forceinline__ void quantize_block_warp(float x, uint8_t* dst, int lane, uint8_t* dst2 = nullptr) {
     if constexpr (T == kQ8_0) {
         float amax = warp_max_abs(fabsf(x));
         float d = __fdiv_rn(amax, 127.0f);
         float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
         int q = (int)roundf(__fmul_rn(x, id));          // ties away from zero (np_roundf)
-        if (lane == 0) store_u16(dst, f2h(d));
+        const uint16_t dh = f2h(d);
+        if (lane == 0) store_u16(dst, dh);
         dst[2 + lane] = (uint8_t)(int8_t)q;
+        if (dst2) {
+            if (lane == 0) store_u16(dst2, dh);
+            dst2[2 + lane] = (uint8_t)(int8_t)q;
+        }
     } else if constexpr (T == kQ4_0 || T == kQ5_0) {
         constexpr float kDiv = T == kQ4_0 ? -8.0f : -16.0f;
         constexpr float kOff = T == kQ4_0 ? 8.5f : 16.5f;
@@ -138,12 +144,18 @@ __device__ __forceinline__ void quantize_block_warp(float x, uint8_t* dst, int l
         int q = (int)truncf(__fadd_rn(__fmul_rn(x, id), kOff));
         q = min(kMax, max(0, q));
         int hi = __shfl_down_sync(0xffffffffu, q, 16);
-        if (lane == 0) store_u16(dst, f2h(d));
-        if constexpr (T == kQ5_0) {
-            uint32_t qh = __ballot_sync(0xffffffffu, (q >> 4) & 1);
-            if (lane == 0) { store_u16(dst + 2, (uint16_t)qh); store_u16(dst + 4, (uint16_t)(qh >> 16)); }
+        uint32_t qh = 0;
+        if constexpr (T == kQ5_0) qh = __ballot_sync(0xffffffffu, (q >> 4) & 1);
+        const uint16_t dh = f2h(d);
+        const uint8_t qs = (uint8_t)((q & 15) | ((hi & 15) << 4));
+        for (int k = 0; k < 2; ++k) {
+            uint8_t* o = k ? dst2 : dst;
+            if (!o) break;
+            if (lane == 0) store_u16(o, dh);
+            if constexpr (T == kQ5_0)
+                if (lane == 0) { store_u16(o + 2, (uint16_t)qh); store_u16(o + 4, (uint16_t)(qh >> 16)); }
+            if (lane < 16) o[BlockTraits<T>::OFF_QS + lane] = qs;
         }
-        if (lane < 16) dst[BlockTraits<T>::OFF_QS + lane] = (uint8_t)((q & 15) | ((hi & 15) << 4));
     } else if constexpr (T == kQ4_1 || T == kQ5_1) {
         constexpr float kDiv = T == kQ4_1 ? 15.0f : 31.0f;
         constexpr int kMax = T == kQ4_1 ? 15 : 31;
@@ -154,16 +166,25 @@ __device__ __forceinline__ void quantize_block_warp(float x, uint8_t* dst, int l
         int q = (int)truncf(__fadd_rn(__fmul_rn(__fsub_rn(x, mn), id), 0.5f));
         q = min(kMax, max(0, q));
         int hi = __shfl_down_sync(0xffffffffu, q, 16);
-        if (lane == 0) { store_u16(dst, f2h(d)); store_u16(dst + 2, f2h(mn)); }
-        if constexpr (T == kQ5_1) {
-            uint32_t qh = __ballot_sync(0xffffffffu, (q >> 4) & 1);
-            if (lane == 0) { store_u16(dst + 4, (uint16_t)qh); store_u16(dst + 6, (uint16_t)(qh >> 16)); }
+        uint32_t qh = 0;
+        if constexpr (T == kQ5_1) qh = __ballot_sync(0xffffffffu, (q >> 4) & 1);
+        const uint16_t dh = f2h(d), mh = f2h(mn);
+        const uint8_t qs = (uint8_t)((q & 15) | ((hi & 15) << 4));
+        for (int k = 0; k < 2; ++k) {
+            uint8_t* o = k ? dst2 : dst;
+            if (!o) break;
+            if (lane == 0) { store_u16(o, dh); store_u16(o + 2, mh); }
+            if constexpr (T == kQ5_1)
+                if (lane == 0) { store_u16(o + 4, (uint16_t)qh); store_u16(o + 6, (uint16_t)(qh >> 16)); }
+            if (lane < 16) o[BlockTraits<T>::OFF_QS + lane] = qs;
         }
-        if (lane < 16) dst[BlockTraits<T>::OFF_QS + lane] = (uint8_t)((q & 15) | ((hi & 15) << 4));
     } else if constexpr (T == kF16) {
-        store_u16(dst + 2 * lane, f2h(x));
+        const uint16_t h = f2h(x);
+        store_u16(dst + 2 * lane, h);
+        if (dst2) store_u16(dst2 + 2 * lane, h);
     } else {  // kF32
         reinterpret_cast<float*>(dst)[lane] = x;
+        if (dst2) reinterpret_cast<float*>(dst2)[lane] = x;
     }
 }
 
@@ -171,8 +192,7 @@ __device__ __forceinline__ void quantize_block_warp(float x, uint8_t* dst, int l
 // consecutive elements for F16/F32) to dst_a and, if non-null, also dst_b.
 template <int T>
 __device__ __forceinline__ void quantize_group_warp2(float x, uint8_t* dst_a, uint8_t* dst_b, int lane) {
-    quantize_block_warp<T>(x, dst_a, lane);
-    if (dst_b) quantize_block_warp<T>(x, dst_b, lane);
+    quantize_block_warp<T>(x, dst_a, lane, dst_b);
 }
 
 // Runtime-type dispatch of the warp quantizer (group = 32 elements).

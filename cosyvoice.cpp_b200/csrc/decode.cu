@@ -114,16 +114,16 @@ cudaError_t launch_decode(cudaStream_t stream, const cvattn_decode_params& p, in
         // persistent pipelined kernel when its ring of stages fits one SM
         const int num_sms = current_sm_count();
         const bool persistent = !(p.flags & CVATTN_DECODE_NOT_PERSISTENT) && num_sms > 0;
-        // Throughput-bound launches (at least kMmaItemsPerSm 64-position items per SM for the
-        // host bound max_kv_len) run the register-resident warp-MMA kernel: fewer
-        // instructions per item, and every warp pair works on its own range.  Latency-bound
-        // launches run the TMEM streaming kernel, whose per-item pipeline is shorter.
-        // CVATTN_DECODE_WARP_MMA / CVATTN_DECODE_TMEM_STREAM force either; the RoPE-fused
-        // step always runs on the streaming kernel.
-        constexpr long kMmaItemsPerSm = 32;
+        // The register-resident warp-MMA kernel takes throughput-bound launches and every
+        // launch of at least two 64-position items per SM (for the host bound max_kv_len)
+        // whose sequences split over at most 32 warp pairs each (dmma::mma_pays); tiny
+        // launches and a few long sequences run the TMEM streaming kernel, whose per-item
+        // pipeline is shorter.  CVATTN_DECODE_WARP_MMA / CVATTN_DECODE_TMEM_STREAM force
+        // either; the RoPE-fused step always runs on the streaming kernel.
         const long items_bound = (long)p.n_seq * ((p.max_kv_len + dmma::kC - 1) / dmma::kC);
         const bool want_mma = (p.flags & CVATTN_DECODE_WARP_MMA) ||
-                              (!(p.flags & CVATTN_DECODE_TMEM_STREAM) && items_bound >= kMmaItemsPerSm * num_sms);
+                              (!(p.flags & CVATTN_DECODE_TMEM_STREAM) &&
+                               dmma::mma_pays(p.k.type, p.v.type, p.n_seq, items_bound, num_sms));
         if (persistent && want_mma && !rope && !(p.flags & CVATTN_DECODE_WIDE_CHUNKS) &&
             dmma::supported_type(p.k.type) && dmma::supported_type(p.v.type) && p.n_seq <= dmma::kMaxSeq) {
             const int chunks_s = (p.max_kv_len + dmma::kC - 1) / dmma::kC;

@@ -58,7 +58,9 @@ constexpr int kEvMin = -3, kEvMax = 6;
 constexpr int kSmemLimit = 227 * 1024;  // dynamic shared memory of one CTA
 constexpr int kMaxTasks = 4 * kMaxPairs;  // merges a CTA can be elected for: two per warp
 constexpr int kMaxMergeRuns = 32;         // runs a CTA-wide merge takes (more: the warp merges alone)
-constexpr int kMergeBatch = 16;           // runs whose (max, sum) and outputs a merging thread loads at once
+constexpr int kMergeBatch = 16;
+constexpr long kLatencyItemsPerSm = 16;   // launches with at most this many items per SM ...
+constexpr int kLatencyPairs = 4;          // ... run this many warp pairs per CTA           // runs whose (max, sum) and outputs a merging thread loads at once
 
 // A merge the CTA was elected for: the runs of (sequence seq, KV head g), whose
 // nruns workspace slots are listed at int offset `slots` of the scale tables.
@@ -508,6 +510,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
     int cseq = 0, cchunk = 0;
     if (n_local > 0) dpipe::item_of(pref, n_seq, lo, cseq, cchunk);
     int qseq = -1;
+    float xk_new[2] = {0.0f, 0.0f}, xv_new[2] = {0.0f, 0.0f};
 
     auto load_q = [&](int sq) {
         float x[2][8];
@@ -564,6 +567,15 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
         const uint8_t* Kst = ring + s * L.stage + g * headK;
         const uint8_t* Vst = ring + s * L.stage + L.vofs + g * headV;
         if (seq != qseq) {
+            // the step's new K/V row of this sequence and KV head (fused append), loaded with Q
+            // so its latency is not paid at the sequence's last chunk
+            if (a.k_new) {
+#pragma unroll
+                for (int b = 0; b < 2; ++b) {
+                    xk_new[b] = a.k_new[(int64_t)seq * 2 * kD + g * kD + b * 32 + lane];
+                    xv_new[b] = a.v_new[(int64_t)seq * 2 * kD + g * kD + b * 32 + lane];
+                }
+            }
             load_q(seq);
             qseq = seq;
         }
@@ -579,13 +591,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
             const uint8_t* vb = a.v_seq_ptrs ? reinterpret_cast<const uint8_t*>(a.v_seq_ptrs[seq]) : a.v_base + seq * a.v_nb2;
             const int rr = len - 1 - p0;
 #pragma unroll
-            for (int b = 0; b < 2; ++b) {
-                const float xk = a.k_new[(int64_t)seq * 2 * kD + g * kD + b * 32 + lane];
-                const float xv = a.v_new[(int64_t)seq * 2 * kD + g * kD + b * 32 + lane];
-                quantize_block_warp<KT>(xk, const_cast<uint8_t*>(Kst) + rr * rowK + b * GBK, lane);
-                quantize_block_warp<KT>(xk, const_cast<uint8_t*>(kb) + (int64_t)(len - 1) * rowK + g * headK + b * GBK, lane);
-                quantize_block_warp<VT>(xv, const_cast<uint8_t*>(Vst) + rr * rowV + b * GBV, lane);
-                quantize_block_warp<VT>(xv, const_cast<uint8_t*>(vb) + (int64_t)(len - 1) * rowV + g * headV + b * GBV, lane);
+            for (int b = 0; b < 2; ++b) {  // one quantization, stored into the slot and the cache
+                quantize_block_warp<KT>(xk_new[b], const_cast<uint8_t*>(Kst) + rr * rowK + b * GBK, lane,
+                                        const_cast<uint8_t*>(kb) + (int64_t)(len - 1) * rowK + g * headK + b * GBK);
+                quantize_block_warp<VT>(xv_new[b], const_cast<uint8_t*>(Vst) + rr * rowV + b * GBV, lane,
+                                        const_cast<uint8_t*>(vb) + (int64_t)(len - 1) * rowV + g * headV + b * GBV);
             }
             fence_proxy_async_smem();  // the slot is later overwritten by the bulk copies
             __syncwarp();
@@ -944,6 +954,36 @@ inline int max_pairs(int k_type, int v_type) {
     int p = kMaxPairs;
     while (p > 1 && Smem(rowK, rowV, p, k_min, v_min).total > kSmemLimit) --p;
     return p;
+}
+
+// Launch shape for `items` 64-position items: warp pairs per CTA and CTAs.  As many pairs as
+// fit (at most one per item per SM); latency-bound launches (at most kLatencyItemsPerSm items
+// per SM) take at most kLatencyPairs: with more, a sequence splits into more runs and the pairs
+// contend for issue slots, and with fewer the CTA is small enough to share its SM with the next
+// launch's (measured on the 24-layer decode step, 7.7 items per SM: 6 pairs 24.7 us per layer,
+// 4 pairs 22.7, 3 or 2 pairs 28-29).
+inline void launch_shape(int k_type, int v_type, long items, int n_sms, int& pairs, int& grid) {
+    pairs = max_pairs(k_type, v_type);
+    const long per_sm = (items + n_sms - 1) / n_sms;
+    if (per_sm < pairs) pairs = (int)(per_sm > 0 ? per_sm : 1);
+    if (per_sm <= kLatencyItemsPerSm && pairs > kLatencyPairs) pairs = kLatencyPairs;
+    const long ctas_needed = (items + pairs - 1) / pairs;
+    grid = (int)(ctas_needed < n_sms ? (ctas_needed > 0 ? ctas_needed : 1) : n_sms);
+}
+
+// Whether the warp-MMA kernel should take a launch of n_seq sequences and `items` items (the
+// host bound): throughput-bound launches (kMmaItemsPerSm items per SM or more), and launches
+// of at least two items per SM whose sequences span at most kMaxMergeRuns pairs each, so that
+// every merge runs CTA-wide.  (Measured, one layer, per launch: 148 x 384 14.1 vs 15.5 us on
+// the streaming kernel, the 64-sequence decode mix 21.3 vs 22.9, 32 x 4096 24.7 vs 27.1; but
+// 16 x 4096, a sequence over ~37 pairs, 43.0 vs 25.2, and 2 x 2048 29.9 vs 25.2.)
+constexpr long kMmaItemsPerSm = 32;
+inline bool mma_pays(int k_type, int v_type, long n_seq, long items, int n_sms) {
+    if (items >= kMmaItemsPerSm * n_sms) return true;
+    if (n_seq <= 0 || items < 2L * n_sms) return false;
+    int pairs = 1, grid = 1;
+    launch_shape(k_type, v_type, items, n_sms, pairs, grid);
+    return (long)grid * pairs / n_seq + 1 <= kMaxMergeRuns;
 }
 
 }  // namespace dmma

@@ -17,12 +17,8 @@ static cudaError_t run(cudaStream_t s, const Args& a, int n_sms) {
     auto fn = decode_mma_kernel<KT, VT>;
     const int rowK = (int)type_row_bytes(KT, 2 * kD), rowV = (int)type_row_bytes(VT, 2 * kD);
     const long items = (long)a.n_seq * ((a.max_kv_len + kC - 1) / kC);
-    int pairs = max_pairs(KT, VT);
-    const long per_sm = (items + n_sms - 1) / n_sms;
-    if (per_sm < pairs) pairs = (int)(per_sm > 0 ? per_sm : 1);
-
-    const long ctas_needed = (items + pairs - 1) / pairs;
-    const int grid = (int)(ctas_needed < n_sms ? (ctas_needed > 0 ? ctas_needed : 1) : n_sms);
+    int pairs = 1, grid = 1;
+    launch_shape(KT, VT, items, n_sms, pairs, grid);
     const int smem = Smem(rowK, rowV, pairs, BlockTraits<KT>::HAS_MIN, BlockTraits<VT>::HAS_MIN).total;
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
