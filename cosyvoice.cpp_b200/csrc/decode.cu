@@ -119,12 +119,12 @@ cudaError_t launch_decode(cudaStream_t stream, const cvattn_decode_params& p, in
         // whose sequences split over at most 32 warp pairs each (dmma::mma_pays); tiny
         // launches and a few long sequences run the TMEM streaming kernel, whose per-item
         // pipeline is shorter.  CVATTN_DECODE_WARP_MMA / CVATTN_DECODE_TMEM_STREAM force
-        // either; the RoPE-fused step always runs on the streaming kernel.
+        // either.  Both apply the RoPE of the fused step.
         const long items_bound = (long)p.n_seq * ((p.max_kv_len + dmma::kC - 1) / dmma::kC);
         const bool want_mma = (p.flags & CVATTN_DECODE_WARP_MMA) ||
                               (!(p.flags & CVATTN_DECODE_TMEM_STREAM) &&
                                dmma::mma_pays(p.k.type, p.v.type, p.n_seq, items_bound, num_sms));
-        if (persistent && want_mma && !rope && !(p.flags & CVATTN_DECODE_WIDE_CHUNKS) &&
+        if (persistent && want_mma && !(p.flags & CVATTN_DECODE_WIDE_CHUNKS) &&
             dmma::supported_type(p.k.type) && dmma::supported_type(p.v.type) && p.n_seq <= dmma::kMaxSeq) {
             const int chunks_s = (p.max_kv_len + dmma::kC - 1) / dmma::kC;
             Args b = a;
@@ -162,7 +162,7 @@ cudaError_t launch_decode(cudaStream_t stream, const cvattn_decode_params& p, in
             default: break;
             }
         }
-        if (a.rope_n_dims > 0) return cudaErrorNotSupported;  // only the streaming kernel applies a RoPE
+        if (a.rope_n_dims > 0) return cudaErrorNotSupported;  // only the two kernels above apply a RoPE
         if (persistent && dpipe::supported_type(p.k.type) &&
             dpipe::supported_type(p.v.type) && p.n_seq <= dpipe::kMaxSeq &&
             dpipe::smem_bytes(p.k.type, p.v.type) <= 227 * 1024) {

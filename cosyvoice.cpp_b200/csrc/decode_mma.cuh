@@ -512,7 +512,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
     int qseq = -1;
     float xk_new[2] = {0.0f, 0.0f}, xv_new[2] = {0.0f, 0.0f};
 
-    auto load_q = [&](int sq) {
+    // RoPE fused into the step (cvattn_decode_rope; n_dims = head_dim = 64): Q and the new K row
+    // turn by the new token's position, as ggml_rope_ext (src/cosyvoice-llm.cpp:56-57); the
+    // (cos, sin) of pair k comes from lane k (one sincosf per lane and sequence).
+    const RopeDev rope{a.rope_mode, a.rope_n_dims, kD, a.rope_theta_scale, a.rope_freq_scale, a.rope_attn_factor};
+    auto load_q = [&](int sq, float2 rcs) {
         float x[2][8];
         float am = 0.0f;
         if (head_ok) {
@@ -530,8 +534,6 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
                     x[b][0] = f0.x; x[b][1] = f0.y; x[b][2] = f1.x; x[b][3] = f1.y;
                     x[b][4] = f0.z; x[b][5] = f0.w; x[b][6] = f1.z; x[b][7] = f1.w;
                 }
-#pragma unroll
-                for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(x[b][i]));
             }
         } else {
 #pragma unroll
@@ -539,6 +541,33 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
 #pragma unroll
                 for (int i = 0; i < 8; ++i) x[b][i] = 0.0f;
         }
+        if (rope.n_dims > 0) {
+            if (rope.mode & 2) {  // NEOX: element e of block 0 pairs with element e of block 1 (pair k = e)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int k = kelem<KT>(tig, i);
+                    const float2 cs = make_float2(__shfl_sync(0xffffffffu, rcs.x, k), __shfl_sync(0xffffffffu, rcs.y, k));
+                    const float a0 = x[0][i], a1 = x[1][i];
+                    x[0][i] = rope_rotate(a0, a1, cs, true);
+                    x[1][i] = rope_rotate(a1, a0, cs, false);
+                }
+            } else {  // NORMAL: elements 2k and 2k + 1 are this lane's entries i and i + 1 (i even)
+#pragma unroll
+                for (int b = 0; b < 2; ++b)
+#pragma unroll
+                    for (int i = 0; i < 8; i += 2) {
+                        const int k = (32 * b + kelem<KT>(tig, i)) >> 1;
+                        const float2 cs = make_float2(__shfl_sync(0xffffffffu, rcs.x, k), __shfl_sync(0xffffffffu, rcs.y, k));
+                        const float a0 = x[b][i], a1 = x[b][i + 1];
+                        x[b][i] = rope_rotate(a0, a1, cs, true);
+                        x[b][i + 1] = rope_rotate(a1, a0, cs, false);
+                    }
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < 2; ++b)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(x[b][i]));
         am = quad_max(am);
         const int ex = dtc::norm_exp(am);
         const float sc = pow2f(ex);
@@ -567,6 +596,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
         const uint8_t* Kst = ring + s * L.stage + g * headK;
         const uint8_t* Vst = ring + s * L.stage + L.vofs + g * headV;
         if (seq != qseq) {
+            float2 rcs = make_float2(1.0f, 0.0f);  // (cos, sin) of pair k = lane at position len - 1
+            if (rope.n_dims > 0) rcs = rope_cs(rope, rope_theta(rope, len - 1, lane));
             // the step's new K/V row of this sequence and KV head (fused append), loaded with Q
             // so its latency is not paid at the sequence's last chunk
             if (a.k_new) {
@@ -575,8 +606,23 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
                     xk_new[b] = a.k_new[(int64_t)seq * 2 * kD + g * kD + b * 32 + lane];
                     xv_new[b] = a.v_new[(int64_t)seq * 2 * kD + g * kD + b * 32 + lane];
                 }
+                if (rope.n_dims > 0) {  // the new K row turns by position len - 1
+                    if (rope.mode & 2) {  // NEOX: element lane of block 0 pairs with element lane of block 1
+                        const float a0 = xk_new[0], a1 = xk_new[1];
+                        xk_new[0] = rope_rotate(a0, a1, rcs, true);
+                        xk_new[1] = rope_rotate(a1, a0, rcs, false);
+                    } else {  // NORMAL: elements lane and lane ^ 1 of block b, pair 16 b + lane / 2
+#pragma unroll
+                        for (int b = 0; b < 2; ++b) {
+                            const float partner = __shfl_xor_sync(0xffffffffu, xk_new[b], 1);
+                            const int k = 16 * b + (lane >> 1);
+                            const float2 cs = make_float2(__shfl_sync(0xffffffffu, rcs.x, k), __shfl_sync(0xffffffffu, rcs.y, k));
+                            xk_new[b] = rope_rotate(xk_new[b], partner, cs, (lane & 1) == 0);
+                        }
+                    }
+                }
             }
-            load_q(seq);
+            load_q(seq, rcs);
             qseq = seq;
         }
         // raw rows of item t have landed (lane 0 waits, the warp follows)

@@ -113,9 +113,11 @@ def build_cache(cv, cuda, oracle, kt, vt, lens, rng, cap, unit, n_dims, m, base)
 
 @pytest.mark.parametrize("kname,vname", [("q8_0", "q8_0"), ("q4_1", "q5_1"), ("q8_0", "q4_0")])
 @pytest.mark.parametrize("mode", ["neox", "normal"])
-def test_decode_rope_fused(ctx, cv, cuda, oracle, kname, vname, mode):
+@pytest.mark.parametrize("path", ["warp_mma", "tmem_stream"])
+def test_decode_rope_fused(ctx, cv, cuda, oracle, kname, vname, mode, path):
     """One decode step with the RoPE of Q and the new K row fused in: Q and k_new turn
-    by kv_len - 1, the rotated k_new (and v_new) are appended, then attention."""
+    by kv_len - 1, the rotated k_new (and v_new) are appended, then attention; on both
+    persistent kernels that apply it."""
     torch = cuda
     kt, vt = cv.TYPE_BY_NAME[kname], cv.TYPE_BY_NAME[vname]
     m = cv.ROPE_NEOX if mode == "neox" else cv.ROPE_NORMAL
@@ -133,7 +135,7 @@ def test_decode_rope_fused(ctx, cv, cuda, oracle, kname, vname, mode):
     out = torch.empty_like(qt)
     rp = cv.rope_params(m, D, D, base)
     dec = cv.Decoder(ctx, kd, vd, n, HQ, cap, qt, out, kl, k_new=torch.tensor(kn, device="cuda"),
-                     v_new=torch.tensor(vn, device="cuda"), rope=rp)
+                     v_new=torch.tensor(vn, device="cuda"), rope=rp, **{path: True})
     dec()
     got = out.cpu().numpy()
     assert ctx.sync_status()[0] == 0
@@ -169,7 +171,7 @@ def test_decode_rope_unsupported_paths(ctx, cv, cuda):
     out = torch.empty_like(q)
     kl = torch.full((n,), 10, dtype=torch.int32, device="cuda")
     rp = cv.rope_params(cv.ROPE_NEOX, D, D, THETA)
-    with pytest.raises(cv.CvattnError):  # f16 K: not the streaming kernel
+    with pytest.raises(cv.CvattnError):  # f16 K: neither persistent kernel
         cv.Decoder(ctx, kd, vd, n, HQ, cap, q, out, kl, rope=rp)()
     kb, kd = cv.alloc_kv(cv.Q8_0, HKV, D, cap, n)
     vb, vd = cv.alloc_kv(cv.Q8_0, HKV, D, cap, n)
