@@ -283,10 +283,11 @@ cvattn_status cvattn_decode_noalloc(cvattn_context* ctx, void* stream, const cva
 /* cvattn_decode with the RoPE of the decode step fused in: Q and the appended
  * K row of sequence s turn by position kv_len[s] - 1 (the ggml_rope_ext calls
  * of src/cosyvoice-llm.cpp:56-57 before update_cache and attention_forward).
- * Runs on the default streaming kernel, so it needs block-quantized K and V,
- * 2 KV heads, head_dim 64, at most 512 sequences, no flag that selects
- * another kernel, and a per-head rope (unit_len = n_dims = head_dim);
- * otherwise CVATTN_ERR_UNSUPPORTED (use cvattn_rope, then cvattn_decode). */
+ * Runs on either persistent decode kernel (warp-MMA or streaming, the
+ * dispatcher's choice), so it needs block-quantized K and V, 2 KV heads,
+ * head_dim 64, at most 512 sequences, no flag that selects another kernel,
+ * and a per-head rope (unit_len = n_dims = head_dim); otherwise
+ * CVATTN_ERR_UNSUPPORTED (use cvattn_rope, then cvattn_decode). */
 cvattn_status cvattn_decode_rope(cvattn_context* ctx, void* stream, const cvattn_decode_params* p,
                                  const cvattn_rope_params* rope);
 
