@@ -58,7 +58,7 @@ constexpr int kEvMin = -3, kEvMax = 6;
 constexpr int kSmemLimit = 227 * 1024;  // dynamic shared memory of one CTA
 constexpr int kMaxTasks = 4 * kMaxPairs;  // merges a CTA can be elected for: two per warp
 constexpr int kMaxMergeRuns = 32;         // runs a CTA-wide merge takes (more: the warp merges alone)
-constexpr int kMergeBatch = 16;
+constexpr int kMergeBatch = 10;
 constexpr long kLatencyItemsPerSm = 16;   // launches with at most this many items per SM ...
 constexpr int kLatencyPairs = 4;          // ... run this many warp pairs per CTA           // runs whose (max, sum) and outputs a merging thread loads at once
 
@@ -262,6 +262,30 @@ __device__ __forceinline__ long long cut_at(long long bb, long long n, long long
     const unsigned long long x = (unsigned long long)(bb * n);
     if ((x >> 32) == 0 && (P >> 32) == 0) return (long long)((uint32_t)x / (uint32_t)P);
     return (long long)(x / (unsigned long long)P);
+}
+
+// One batch of a log-sum-exp merge: fold the first n (<= K) of the runs' (max, sum) and
+// outputs into the running (M, Ls, acc), rescaling them to the batch's new max.
+template <int K>
+__device__ __forceinline__ void lse_batch(const float2 (&ml)[K], const float4 (&v)[K], int n, float& M, float& Ls,
+                                          float4& acc) {
+    if (n <= 0) return;
+    float bm = M;
+#pragma unroll
+    for (int j = 0; j < K; ++j)
+        if (j < n) bm = fmaxf(bm, ml[j].x);
+    const float rs = (M == -INFINITY) ? 0.0f : fast_exp2(M - bm);
+    Ls *= rs;
+    acc.x *= rs; acc.y *= rs; acc.z *= rs; acc.w *= rs;
+    M = bm;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+        if (j >= n) break;
+        const float wj = ml[j].x == -INFINITY ? 0.0f : fast_exp2(ml[j].x - M);
+        Ls = fmaf(wj, ml[j].y, Ls);
+        acc.x = fmaf(wj, v[j].x, acc.x); acc.y = fmaf(wj, v[j].y, acc.y);
+        acc.z = fmaf(wj, v[j].z, acc.z); acc.w = fmaf(wj, v[j].w, acc.w);
+    }
 }
 
 // Log-sum-exp merge of the runs of (sequence seq, KV head group qh0 / G) by one
@@ -893,7 +917,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
     // ---- The merges this CTA's warps were elected for (the last writer of a sequence's runs for
     // one KV head), done by every thread of the CTA: the elected warp lists the run slots in its
     // scale table (free after the loop) and posts a task; after one CTA barrier, thread =
-    // (task, head, 4 dims) loads up to kMergeBatch runs' (max, sum) and outputs at once, so a sequence
+    // (task, head, 4 dims) loads up to kMergeBatch runs' (max, sum) and outputs at once, for two items together, so a sequence
     // split over many pairs costs a round or two of L2 loads instead of one warp's many.  (A
     // sequence over more than kMaxMergeRuns pairs, and every merge of a one-pair CTA, whose two
     // warps would otherwise share 64 threads, is merged by its warp alone.)
@@ -923,50 +947,59 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
     __syncthreads();  // tasks posted; the electing acquires precede every thread's partial loads
     {
         const int n_tasks = *mcount;
-        for (int w = tid; w < n_tasks * G * (kD / 4); w += blockDim.x) {
-            const MergeTask T = tasks[w / (G * (kD / 4))];
-            const int h = (w / (kD / 4)) % G, dq = (w % (kD / 4)) * 4;
-            const int qh = T.g * G + h, R = T.nruns;
-            const int* slots = slot_tab + T.slots;
-            const float* seq_ml = a.ws_ml + ((int64_t)T.seq * a.ws_chunks) * Hq * 2;
-            const float* seq_o = a.ws_o + ((int64_t)T.seq * a.ws_chunks) * Hq * kD;
-            float M = -INFINITY, Ls = 0.0f;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int r0 = 0; r0 < R; r0 += kMergeBatch) {
-                float2 ml[kMergeBatch];
-                float4 v[kMergeBatch];
+        // thread = two merge items (task, head, 4 dims) at once, so the loads of both are in flight
+        // together: a CTA elected for several sequences pays half the rounds of L2 loads
+        const int n_work = n_tasks * G * (kD / 4);
+        auto item_of = [&](int w, MergeTask& T, int& h, int& dq) {
+            T = tasks[w / (G * (kD / 4))];
+            h = (w / (kD / 4)) % G;
+            dq = (w % (kD / 4)) * 4;
+        };
+        for (int w0 = tid; w0 < n_work; w0 += 2 * blockDim.x) {
+            const int w1 = w0 + blockDim.x;
+            const bool two = w1 < n_work;
+            MergeTask TA, TB;
+            int hA, dqA, hB, dqB;
+            item_of(w0, TA, hA, dqA);
+            item_of(two ? w1 : w0, TB, hB, dqB);
+            const int qhA = TA.g * G + hA, qhB = TB.g * G + hB;
+            const float* mlA = a.ws_ml + ((int64_t)TA.seq * a.ws_chunks) * Hq * 2 + qhA * 2;
+            const float* oA = a.ws_o + ((int64_t)TA.seq * a.ws_chunks) * Hq * kD + qhA * kD + dqA;
+            const float* mlB = a.ws_ml + ((int64_t)TB.seq * a.ws_chunks) * Hq * 2 + qhB * 2;
+            const float* oB = a.ws_o + ((int64_t)TB.seq * a.ws_chunks) * Hq * kD + qhB * kD + dqB;
+            float MA = -INFINITY, LA = 0.0f, MB = -INFINITY, LB = 0.0f;
+            float4 accA = make_float4(0.f, 0.f, 0.f, 0.f), accB = accA;
+            const int RR = TA.nruns > TB.nruns ? TA.nruns : TB.nruns;
+            for (int r0 = 0; r0 < RR; r0 += kMergeBatch) {
+                float2 ma[kMergeBatch], mb[kMergeBatch];
+                float4 va[kMergeBatch], vb[kMergeBatch];
 #pragma unroll
                 for (int j = 0; j < kMergeBatch; ++j) {
-                    const int cc = slots[min(r0 + j, R - 1)];
-                    ml[j] = __ldcg(reinterpret_cast<const float2*>(seq_ml + ((int64_t)cc * Hq + qh) * 2));
-                    v[j] = dpipe::ldcg_f4(seq_o + ((int64_t)cc * Hq + qh) * kD + dq);
+                    const int ca = slot_tab[TA.slots + min(r0 + j, TA.nruns - 1)];
+                    const int cb = slot_tab[TB.slots + min(r0 + j, TB.nruns - 1)];
+                    ma[j] = __ldcg(reinterpret_cast<const float2*>(mlA + (int64_t)ca * Hq * 2));
+                    va[j] = dpipe::ldcg_f4(oA + (int64_t)ca * Hq * kD);
+                    mb[j] = __ldcg(reinterpret_cast<const float2*>(mlB + (int64_t)cb * Hq * 2));
+                    vb[j] = dpipe::ldcg_f4(oB + (int64_t)cb * Hq * kD);
                 }
-                float bm = M;
-#pragma unroll
-                for (int j = 0; j < kMergeBatch; ++j)
-                    if (r0 + j < R) bm = fmaxf(bm, ml[j].x);
-                const float rs = (M == -INFINITY) ? 0.0f : fast_exp2(M - bm);
-                Ls *= rs;
-                acc.x *= rs; acc.y *= rs; acc.z *= rs; acc.w *= rs;
-                M = bm;
-#pragma unroll
-                for (int j = 0; j < kMergeBatch; ++j) {
-                    if (r0 + j >= R) break;
-                    const float wj = ml[j].x == -INFINITY ? 0.0f : fast_exp2(ml[j].x - M);
-                    Ls = fmaf(wj, ml[j].y, Ls);
-                    acc.x = fmaf(wj, v[j].x, acc.x); acc.y = fmaf(wj, v[j].y, acc.y);
-                    acc.z = fmaf(wj, v[j].z, acc.z); acc.w = fmaf(wj, v[j].w, acc.w);
-                }
+                lse_batch<kMergeBatch>(ma, va, TA.nruns - r0, MA, LA, accA);
+                lse_batch<kMergeBatch>(mb, vb, TB.nruns - r0, MB, LB, accB);
             }
-            float* out = a.out + (int64_t)T.seq * a.out_seq_stride;
-            const float inv = emit_partial ? 1.0f : 1.0f / Ls;
-            *reinterpret_cast<float4*>(out + qh * kD + dq) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-            if (dq == 0) {
-                if (emit_partial) {
-                    a.partial_ml[((int64_t)T.seq * Hq + qh) * 2] = M;
-                    a.partial_ml[((int64_t)T.seq * Hq + qh) * 2 + 1] = Ls;
+            for (int k = 0; k < (two ? 2 : 1); ++k) {
+                const MergeTask& T = k ? TB : TA;
+                const int h = k ? hB : hA, dq = k ? dqB : dqA, qh = k ? qhB : qhA;
+                const float Mk = k ? MB : MA, Lk = k ? LB : LA;
+                const float4 acc = k ? accB : accA;
+                float* out = a.out + (int64_t)T.seq * a.out_seq_stride;
+                const float inv = emit_partial ? 1.0f : 1.0f / Lk;
+                *reinterpret_cast<float4*>(out + qh * kD + dq) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+                if (dq == 0) {
+                    if (emit_partial) {
+                        a.partial_ml[((int64_t)T.seq * Hq + qh) * 2] = Mk;
+                        a.partial_ml[((int64_t)T.seq * Hq + qh) * 2 + 1] = Lk;
+                    }
+                    if (h == 0) a.ws_cnt[(int64_t)T.seq * 2 + T.g] = 0u;  // the ticket is not read again in this launch
                 }
-                if (h == 0) a.ws_cnt[(int64_t)T.seq * 2 + T.g] = 0u;  // the ticket is not read again in this launch
             }
         }
     }
