@@ -537,14 +537,14 @@ def decode_kernel_name(n_seq: int, items: int, n_sms: int, max_pairs: int = 6) -
     csrc/decode_mma.cuh, for type pairs that fit six warp pairs per CTA)."""
     if items >= 32 * n_sms:
         return "decode_mma_kernel"
-    if n_seq <= 0 or items < 2 * n_sms:
+    if n_seq <= 0 or items < n_sms:
         return "decode_stream_kernel"
     per_sm = -(-items // n_sms)
     pairs = min(max_pairs, max(per_sm, 1))
     if per_sm <= 16:
         pairs = min(pairs, 4)
     grid = min(n_sms, max(-(-items // pairs), 1))
-    return "decode_mma_kernel" if grid * pairs // n_seq + 1 <= 32 else "decode_stream_kernel"
+    return "decode_mma_kernel" if grid * pairs // n_seq + 1 <= 128 else "decode_stream_kernel"
 
 
 def run_decode_cfg4_sharded(torch, cv, ctx, rank: int, world: int, dist, reps: int = 10) -> dict:

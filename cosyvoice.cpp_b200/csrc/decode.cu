@@ -114,11 +114,11 @@ cudaError_t launch_decode(cudaStream_t stream, const cvattn_decode_params& p, in
         // persistent pipelined kernel when its ring of stages fits one SM
         const int num_sms = current_sm_count();
         const bool persistent = !(p.flags & CVATTN_DECODE_NOT_PERSISTENT) && num_sms > 0;
-        // The register-resident warp-MMA kernel takes throughput-bound launches and every
-        // launch of at least two 64-position items per SM (for the host bound max_kv_len)
-        // whose sequences split over at most 32 warp pairs each (dmma::mma_pays); tiny
-        // launches and a few long sequences run the TMEM streaming kernel, whose per-item
-        // pipeline is shorter.  CVATTN_DECODE_WARP_MMA / CVATTN_DECODE_TMEM_STREAM force
+        // The register-resident warp-MMA kernel takes every launch of at least one
+        // 64-position item per SM (for the host bound max_kv_len) whose sequences split over
+        // at most 128 warp pairs each, and every throughput-bound launch (dmma::mma_pays);
+        // smaller launches (one to a few long sequences) run the TMEM streaming kernel, whose
+        // per-item pipeline is shorter.  CVATTN_DECODE_WARP_MMA / CVATTN_DECODE_TMEM_STREAM force
         // either.  Both apply the RoPE of the fused step.
         const long items_bound = (long)p.n_seq * ((p.max_kv_len + dmma::kC - 1) / dmma::kC);
         const bool want_mma = (p.flags & CVATTN_DECODE_WARP_MMA) ||

@@ -57,7 +57,7 @@ constexpr float kLazyLog2 = 8.0f;
 constexpr int kEvMin = -3, kEvMax = 6;
 constexpr int kSmemLimit = 227 * 1024;  // dynamic shared memory of one CTA
 constexpr int kMaxTasks = 4 * kMaxPairs;  // merges a CTA can be elected for: two per warp
-constexpr int kMaxMergeRuns = 32;         // runs a CTA-wide merge takes (more: the warp merges alone)
+constexpr int kMaxMergeRuns = 64;         // runs a CTA-wide merge takes (more: the warp merges alone)
 constexpr int kMergeBatch = 10;
 constexpr long kLatencyItemsPerSm = 16;   // launches with at most this many items per SM ...
 constexpr int kLatencyPairs = 4;          // ... run this many warp pairs per CTA           // runs whose (max, sum) and outputs a merging thread loads at once
@@ -934,15 +934,19 @@ __global__ void __launch_bounds__(kMaxThreads, 1) decode_mma_kernel(const Args a
             if (lane == 0) a.ws_cnt[(int64_t)sq * 2 + g] = 0u;
             continue;
         }
-        int c = -1;  // lane r: the slot of pair b0 + r's run (none when the pair has no items)
-        if (lane <= b1 - b0) {
-            const long long blo = cut_at(b0 + lane, n_items, P), bhi = cut_at(b0 + lane + 1, n_items, P);
-            if (bhi > blo) c = (int)((blo > ps ? blo : ps) - ps);
-        }
-        const uint32_t vm = __ballot_sync(0xffffffffu, c >= 0);
         const int off = (warp * L.scl_warp) / 4 + i * kMaxMergeRuns;
-        if (c >= 0) slot_tab[off + __popc(vm & ((1u << lane) - 1u))] = c;
-        if (lane == 0) tasks[atomicAdd(mcount, 1)] = MergeTask{sq, g, __popc(vm), off};
+        int nr = 0;  // the slots of the pairs' runs, listed 32 pairs at a time (a pair without items has none)
+        for (int base = 0; base <= b1 - b0; base += 32) {
+            int c = -1;
+            if (base + lane <= b1 - b0) {
+                const long long blo = cut_at(b0 + base + lane, n_items, P), bhi = cut_at(b0 + base + lane + 1, n_items, P);
+                if (bhi > blo) c = (int)((blo > ps ? blo : ps) - ps);
+            }
+            const uint32_t vm = __ballot_sync(0xffffffffu, c >= 0);
+            if (c >= 0) slot_tab[off + nr + __popc(vm & ((1u << lane) - 1u))] = c;
+            nr += __popc(vm);
+        }
+        if (lane == 0) tasks[atomicAdd(mcount, 1)] = MergeTask{sq, g, nr, off};
     }
     __syncthreads();  // tasks posted; the electing acquires precede every thread's partial loads
     {
@@ -1051,18 +1055,19 @@ inline void launch_shape(int k_type, int v_type, long items, int n_sms, int& pai
 }
 
 // Whether the warp-MMA kernel should take a launch of n_seq sequences and `items` items (the
-// host bound): throughput-bound launches (kMmaItemsPerSm items per SM or more), and launches
-// of at least two items per SM whose sequences span at most kMaxMergeRuns pairs each, so that
-// every merge runs CTA-wide.  (Measured, one layer, per launch: 148 x 384 14.1 vs 15.5 us on
-// the streaming kernel, the 64-sequence decode mix 21.3 vs 22.9, 32 x 4096 24.7 vs 27.1; but
-// 16 x 4096, a sequence over ~37 pairs, 43.0 vs 25.2, and 2 x 2048 29.9 vs 25.2.)
+// host bound): throughput-bound launches (kMmaItemsPerSm items per SM or more), and every
+// launch of at least one item per SM whose sequences span at most 2 kMaxMergeRuns pairs each.
+// (Measured, one layer, per launch, against the streaming kernel: the 64-sequence decode
+// mix 20.9 vs 22.9 us, 148 x 64 6.9 vs 8.2, 64 x 256 10.3 vs 11.7, 3 x 4096 29.1 vs 43.3,
+// 8 x 4096 26.4 vs 30.7, 16 x 4096 22.0 vs 24.8; below one item per SM the streaming kernel
+// wins: 1 x 4096 50.9 vs 42.8, 2 x 4096 51.2 vs 45.5, 1 x 8192 93.6 vs 80.8.)
 constexpr long kMmaItemsPerSm = 32;
 inline bool mma_pays(int k_type, int v_type, long n_seq, long items, int n_sms) {
     if (items >= kMmaItemsPerSm * n_sms) return true;
-    if (n_seq <= 0 || items < 2L * n_sms) return false;
+    if (n_seq <= 0 || items < n_sms) return false;
     int pairs = 1, grid = 1;
     launch_shape(k_type, v_type, items, n_sms, pairs, grid);
-    return (long)grid * pairs / n_seq + 1 <= kMaxMergeRuns;
+    return (long)grid * pairs / n_seq + 1 <= 2 * kMaxMergeRuns;
 }
 
 }  // namespace dmma

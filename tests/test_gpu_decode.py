@@ -358,12 +358,13 @@ def test_decode_running_rescales(ctx, cv, cuda, oracle, kname, vname, path):
 
 
 @pytest.mark.parametrize("path", ["warp_mma", "tmem_stream"])
-@pytest.mark.parametrize("shape", ["one_long", "six_runs_per_cta", "headline_mix"])
+@pytest.mark.parametrize("shape", ["one_long", "six_runs_per_cta", "headline_mix", "eight_long"])
 def test_decode_merge_shapes(ctx, cv, cuda, oracle, path, shape):
-    """Split sequences merged at the end of the launch: one sequence over more than 32
+    """Split sequences merged at the end of the launch: one sequence over more than 64
     warp pairs (merged by its elected warp alone), 148 sequences of six chunks (six runs
-    of a sequence inside one CTA, several merges per CTA), and the headline's mix of 64
-    sequences with lengths in [128, 2048]."""
+    of a sequence inside one CTA, several merges per CTA), the headline's mix of 64
+    sequences with lengths in [128, 2048], and eight sequences of 2048 (each over ~33
+    pairs: CTA-wide merges of more than 32 runs)."""
     torch = cuda
     kt, vt = cv.Q8_0, cv.Q4_0
     rng = np.random.default_rng(53)
@@ -371,6 +372,8 @@ def test_decode_merge_shapes(ctx, cv, cuda, oracle, path, shape):
         lens = [5000, 1, 64, 65, 127]
     elif shape == "six_runs_per_cta":
         lens = [384] * 148
+    elif shape == "eight_long":
+        lens = [2048] * 8
     else:
         lens = np.random.default_rng(0).integers(128, 2049, 64).tolist()
     cap = max(lens)
