@@ -3,8 +3,10 @@
 // (src/cosyvoice-kv-cache.cpp:315-316,321-322), plus the inverse
 // (dequantize rows to f32) used for slot export and tests.
 //
-// One warp handles one 32-element group of one row; blocks are bit-identical
-// to ggml's reference quantizers (see quantize_block_warp in common.cuh).
+// Block-quantized rows without a RoPE: one thread per 32-element block
+// (quantize_block_thread, a sequential scan); f16 / f32 rows and RoPE'd rows:
+// one warp per row, one lane per element (quantize_block_warp in common.cuh).
+// Both are bit-identical to ggml's reference quantizers.
 // HBM-bound: reads 128 B of f32 per group, writes 18-128 B.
 //
 // With a RoPE the K rows are rotated on the way in, as ggml_rope_ext does
@@ -62,6 +64,104 @@ __global__ void __launch_bounds__(256) kv_append_kernel(
     }
 }
 
+// Quantize the 32 values of one block into dst (2-byte aligned) with one thread: the
+// sequential first-occurrence scans of ggml's reference quantizers (gguf-py quants.py
+// Q4_0 :220-252, Q4_1 :254-289, Q5_0 :291-331, Q5_1 :333-376, Q8_0 :378-401) and the
+// same IEEE fp32 operations as quantize_block_warp, so the bytes are the same.
+template <int T>
+__device__ __forceinline__ void quantize_block_thread(const float (&x)[32], uint8_t* dst) {
+    using B = BlockTraits<T>;
+    if constexpr (T == kQ8_0) {
+        float amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(x[j]));
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        store_u16(dst, f2h(d));
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+            const int q0 = (int)roundf(__fmul_rn(x[j], id)), q1 = (int)roundf(__fmul_rn(x[j + 1], id));
+            store_u16(dst + 2 + j, (uint16_t)((q0 & 255) | ((q1 & 255) << 8)));
+        }
+    } else {
+        constexpr bool kMin = B::HAS_MIN, k5 = B::OFF_QH >= 0;
+        constexpr int kMax = k5 ? 31 : 15;
+        float d, lo = 0.0f;
+        if constexpr (kMin) {  // min and max, first occurrence (strict comparisons)
+            float mn = x[0], mx = x[0];
+#pragma unroll
+            for (int j = 1; j < 32; ++j) {
+                if (x[j] < mn) mn = x[j];
+                if (x[j] > mx) mx = x[j];
+            }
+            d = __fdiv_rn(__fsub_rn(mx, mn), k5 ? 31.0f : 15.0f);
+            lo = mn;
+        } else {  // the value of largest magnitude, first occurrence
+            float amax = 0.0f, mx = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (amax < fabsf(x[j])) {
+                    amax = fabsf(x[j]);
+                    mx = x[j];
+                }
+            d = __fdiv_rn(mx, k5 ? -16.0f : -8.0f);
+        }
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        int q[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const int v = kMin ? (int)truncf(__fadd_rn(__fmul_rn(__fsub_rn(x[j], lo), id), 0.5f))
+                               : (int)truncf(__fadd_rn(__fmul_rn(x[j], id), k5 ? 16.5f : 8.5f));
+            q[j] = min(kMax, max(0, v));
+        }
+        store_u16(dst, f2h(d));
+        if constexpr (kMin) store_u16(dst + 2, f2h(lo));
+        if constexpr (k5) {  // bit e of qh: the fifth bit of element e
+            uint32_t qh = 0;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) qh |= (uint32_t)((q[j] >> 4) & 1) << j;
+            store_u16(dst + B::OFF_QH, (uint16_t)qh);
+            store_u16(dst + B::OFF_QH + 2, (uint16_t)(qh >> 16));
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j += 2)  // byte j: element j (low nibble) and element j + 16 (high)
+            store_u16(dst + B::OFF_QS + j, (uint16_t)(((q[j] & 15) | ((q[j + 16] & 15) << 4)) |
+                                                      (((q[j + 1] & 15) | ((q[j + 17] & 15) << 4)) << 8)));
+    }
+}
+
+// Block-quantized append without a RoPE: one thread per 32-element block (row (t, b), block
+// g fastest), its 128 bytes of f32 read as eight 16-byte loads, the block quantized by a
+// sequential scan (no warp reductions): ~5x fewer instructions per block than the warp form.
+constexpr int kAppendBlockThreadsPerSm = 512;  // smallest launch (blocks per SM) that takes this form
+
+template <int T>
+__global__ void __launch_bounds__(256) kv_append_block_kernel(
+    uint8_t* __restrict__ cache, int64_t nb1, int64_t nb2, int64_t capacity, int groups_per_row,
+    const float* __restrict__ src, int64_t src_nb1, int64_t src_nb2,
+    const int32_t* __restrict__ pos, int64_t pos_stride, int n_new, int batch, int* status) {
+    const int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gi >= (int64_t)n_new * batch * groups_per_row) return;
+    const int g = (int)(gi % groups_per_row);
+    const int64_t rw = gi / groups_per_row;  // row (t, b), t fastest
+    const int b = (int)(rw / n_new);
+    const int t = (int)(rw - (int64_t)b * n_new);
+    const int p = pos[t + (int64_t)b * pos_stride];
+    if (p < 0 || p >= capacity) {
+        if (g == 0) record_status(status, kStatusBadPosition);
+        return;
+    }
+    const float4* s4 =
+        reinterpret_cast<const float4*>(reinterpret_cast<const uint8_t*>(src) + t * src_nb1 + b * src_nb2) + 8 * g;
+    float x[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 v = __ldcs(s4 + i);  // read once
+        x[4 * i] = v.x; x[4 * i + 1] = v.y; x[4 * i + 2] = v.z; x[4 * i + 3] = v.w;
+    }
+    quantize_block_thread<T>(x, cache + b * nb2 + (int64_t)p * nb1 + (int64_t)g * group_bytes(T));
+}
+
 // Standalone RoPE: rows of row_len floats (row r at x + r * x_nb1f, out + r * out_nb1f;
 // x may equal out).  One thread per pair (or per unrotated element), so a pair
 // is read before either of its elements is written.
@@ -114,6 +214,30 @@ cudaError_t launch_kv_append(cudaStream_t stream, const cvattn_tensor& c, const 
     if (rows > 0x7fffffffLL) return cudaErrorInvalidValue;
     const unsigned grid = (unsigned)((rows + 7) / 8);
     uint8_t* base = static_cast<uint8_t*>(c.data);
+    // block-quantized caches without a RoPE, f32 rows 16-byte aligned, and enough blocks for at
+    // least 512 threads per SM: a thread per block.  Smaller launches (the LLM's 256-token
+    // prefill calls hold 8,192 blocks) keep a warp per block, which has 32x the threads in flight.
+    const bool block_type = c.type == kQ4_0 || c.type == kQ4_1 || c.type == kQ5_0 || c.type == kQ5_1 || c.type == kQ8_0;
+    const int64_t blocks = rows * groups;
+    if (block_type && rp.n_dims == 0 && blocks >= (int64_t)current_sm_count() * kAppendBlockThreadsPerSm &&
+        ((reinterpret_cast<uintptr_t>(src) | (uintptr_t)src_nb1 | (uintptr_t)src_nb2) & 15) == 0) {
+        const unsigned gridb = (unsigned)((blocks + 255) / 256);
+        if ((blocks + 255) / 256 > 0x7fffffffLL) return cudaErrorInvalidValue;
+#define CVATTN_APPEND_BLOCK_CASE(T)                                                                          \
+    case T:                                                                                                  \
+        kv_append_block_kernel<T><<<gridb, 256, 0, stream>>>(base, c.nb1, c.nb2, c.ne1, groups, src, src_nb1, \
+                                                             src_nb2, pos, pos_stride, n_new, batch, status);  \
+        return cudaGetLastError();
+        switch (c.type) {
+            CVATTN_APPEND_BLOCK_CASE(kQ4_0)
+            CVATTN_APPEND_BLOCK_CASE(kQ4_1)
+            CVATTN_APPEND_BLOCK_CASE(kQ5_0)
+            CVATTN_APPEND_BLOCK_CASE(kQ5_1)
+            CVATTN_APPEND_BLOCK_CASE(kQ8_0)
+        default: break;
+        }
+#undef CVATTN_APPEND_BLOCK_CASE
+    }
 #define CVATTN_APPEND_CASE(T)                                                                              \
     case T:                                                                                                \
         kv_append_kernel<T><<<grid, 256, 0, stream>>>(base, c.nb1, c.nb2, c.ne1, groups, src, src_nb1,     \

@@ -67,6 +67,44 @@ def test_append_random_bit_exact(ctx, cv, cuda, oracle, name, heads, batch, n_ne
         assert np.array_equal(got[b][pnp[b]], exp), f"{name} batch {b}"
 
 
+@pytest.mark.parametrize("name", ["q8_0", "q5_1", "q5_0", "q4_1", "q4_0"])
+def test_append_dit_launch_bit_exact(ctx, cv, cuda, oracle, name):
+    """A DiT-sized append (8 entries x 600 rows of 16 heads x 64: 153,600 blocks) takes the
+    thread-per-block quantizer; its sequential scans must keep ggml's tie rules: the first
+    element of largest magnitude gives q4_0/q5_0 their sign, an all-zero block a zero scale and
+    a constant block a zero range.  One position is out of range: that row is skipped and
+    reported, the rest are written."""
+    torch = cuda
+    t = cv.TYPE_BY_NAME[name]
+    rng = np.random.default_rng(11)
+    batch, n_new, heads = 8, 600, 16
+    row = heads * 64
+    cap = n_new + 50
+    x = rng.standard_normal((batch, n_new, row)).astype(np.float32)
+    blk = x.reshape(-1, 32)
+    sel = rng.random(blk.shape[0])
+    ties = np.nonzero(sel < 0.05)[0]
+    a, b = rng.integers(0, 32, ties.size), rng.integers(0, 32, ties.size)
+    b = np.where(a == b, (b + 1) % 32, b)
+    m = rng.choice([4.0, 7.5], ties.size).astype(np.float32)
+    blk[ties, a] = m                      # +m and -m: whichever comes first sets the sign
+    blk[ties, b] = -m
+    blk[(sel >= 0.05) & (sel < 0.06)] = 0.0
+    blk[(sel >= 0.06) & (sel < 0.07)] = 1.25
+    pnp = np.stack([rng.permutation(cap)[:n_new] for _ in range(batch)]).astype(np.int32)
+    pnp[3, 5] = cap
+    buf, desc = cv.alloc_kv(t, heads, 64, ne1=cap, ne2=batch)
+    cv.kv_append(ctx, desc, torch.tensor(x, device="cuda"), torch.tensor(pnp, device="cuda"))
+    st, detail = ctx.sync_status()
+    assert st == 6 and detail == 1
+    got = buf.view(batch, cap, cv.row_size(t, row)).cpu().numpy()
+    for bb in range(batch):
+        ok = pnp[bb] < cap
+        exp = oracle.quantize(t, x[bb])
+        assert np.array_equal(got[bb][pnp[bb][ok]], exp[ok]), f"{name} batch {bb}"
+    assert not got[3][np.setdiff1d(np.arange(cap), pnp[3])].any()
+
+
 def test_append_bad_position_is_skipped_and_reported(ctx, cv, cuda, oracle):
     torch = cuda
     t = cv.Q8_0
