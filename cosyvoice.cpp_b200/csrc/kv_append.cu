@@ -3,9 +3,9 @@
 // (src/cosyvoice-kv-cache.cpp:315-316,321-322), plus the inverse
 // (dequantize rows to f32) used for slot export and tests.
 //
-// Block-quantized rows without a RoPE: one thread per 32-element block
-// (quantize_block_thread, a sequential scan); f16 / f32 rows and RoPE'd rows:
-// one warp per row, one lane per element (quantize_block_warp in common.cuh).
+// Large launches of 4- and 5-bit rows without a RoPE: one thread per 32-element block
+// (quantize_block_thread, a sequential scan); q8_0, f16 / f32, RoPE'd rows and small
+// launches: one warp per row, one lane per element (quantize_block_warp in common.cuh).
 // Both are bit-identical to ggml's reference quantizers.
 // HBM-bound: reads 128 B of f32 per group, writes 18-128 B.
 //
@@ -64,70 +64,57 @@ __global__ void __launch_bounds__(256) kv_append_kernel(
     }
 }
 
-// Quantize the 32 values of one block into dst (2-byte aligned) with one thread: the
-// sequential first-occurrence scans of ggml's reference quantizers (gguf-py quants.py
-// Q4_0 :220-252, Q4_1 :254-289, Q5_0 :291-331, Q5_1 :333-376, Q8_0 :378-401) and the
-// same IEEE fp32 operations as quantize_block_warp, so the bytes are the same.
+// Quantize the 32 values of one 4- or 5-bit block into dst (2-byte aligned) with one thread:
+// the sequential first-occurrence scans of ggml's reference quantizers (gguf-py quants.py
+// Q4_0 :220-252, Q4_1 :254-289, Q5_0 :291-331, Q5_1 :333-376) and the same IEEE fp32
+// operations as quantize_block_warp, so the bytes are the same.
 template <int T>
 __device__ __forceinline__ void quantize_block_thread(const float (&x)[32], uint8_t* dst) {
     using B = BlockTraits<T>;
-    if constexpr (T == kQ8_0) {
-        float amax = 0.0f;
+    static_assert(T != kQ8_0, "q8_0 appends keep the warp form");
+    constexpr bool kMin = B::HAS_MIN, k5 = B::OFF_QH >= 0;
+    constexpr int kMax = k5 ? 31 : 15;
+    float d, lo = 0.0f;
+    if constexpr (kMin) {  // min and max, first occurrence (strict comparisons)
+        float mn = x[0], mx = x[0];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(x[j]));
-        const float d = __fdiv_rn(amax, 127.0f);
-        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        store_u16(dst, f2h(d));
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-            const int q0 = (int)roundf(__fmul_rn(x[j], id)), q1 = (int)roundf(__fmul_rn(x[j + 1], id));
-            store_u16(dst + 2 + j, (uint16_t)((q0 & 255) | ((q1 & 255) << 8)));
+        for (int j = 1; j < 32; ++j) {
+            if (x[j] < mn) mn = x[j];
+            if (x[j] > mx) mx = x[j];
         }
-    } else {
-        constexpr bool kMin = B::HAS_MIN, k5 = B::OFF_QH >= 0;
-        constexpr int kMax = k5 ? 31 : 15;
-        float d, lo = 0.0f;
-        if constexpr (kMin) {  // min and max, first occurrence (strict comparisons)
-            float mn = x[0], mx = x[0];
+        d = __fdiv_rn(__fsub_rn(mx, mn), k5 ? 31.0f : 15.0f);
+        lo = mn;
+    } else {  // the value of largest magnitude, first occurrence
+        float amax = 0.0f, mx = 0.0f;
 #pragma unroll
-            for (int j = 1; j < 32; ++j) {
-                if (x[j] < mn) mn = x[j];
-                if (x[j] > mx) mx = x[j];
+        for (int j = 0; j < 32; ++j)
+            if (amax < fabsf(x[j])) {
+                amax = fabsf(x[j]);
+                mx = x[j];
             }
-            d = __fdiv_rn(__fsub_rn(mx, mn), k5 ? 31.0f : 15.0f);
-            lo = mn;
-        } else {  // the value of largest magnitude, first occurrence
-            float amax = 0.0f, mx = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (amax < fabsf(x[j])) {
-                    amax = fabsf(x[j]);
-                    mx = x[j];
-                }
-            d = __fdiv_rn(mx, k5 ? -16.0f : -8.0f);
-        }
-        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        int q[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            const int v = kMin ? (int)truncf(__fadd_rn(__fmul_rn(__fsub_rn(x[j], lo), id), 0.5f))
-                               : (int)truncf(__fadd_rn(__fmul_rn(x[j], id), k5 ? 16.5f : 8.5f));
-            q[j] = min(kMax, max(0, v));
-        }
-        store_u16(dst, f2h(d));
-        if constexpr (kMin) store_u16(dst + 2, f2h(lo));
-        if constexpr (k5) {  // bit e of qh: the fifth bit of element e
-            uint32_t qh = 0;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) qh |= (uint32_t)((q[j] >> 4) & 1) << j;
-            store_u16(dst + B::OFF_QH, (uint16_t)qh);
-            store_u16(dst + B::OFF_QH + 2, (uint16_t)(qh >> 16));
-        }
-#pragma unroll
-        for (int j = 0; j < 16; j += 2)  // byte j: element j (low nibble) and element j + 16 (high)
-            store_u16(dst + B::OFF_QS + j, (uint16_t)(((q[j] & 15) | ((q[j + 16] & 15) << 4)) |
-                                                      (((q[j + 1] & 15) | ((q[j + 17] & 15) << 4)) << 8)));
+        d = __fdiv_rn(mx, k5 ? -16.0f : -8.0f);
     }
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    int q[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const int v = kMin ? (int)truncf(__fadd_rn(__fmul_rn(__fsub_rn(x[j], lo), id), 0.5f))
+                           : (int)truncf(__fadd_rn(__fmul_rn(x[j], id), k5 ? 16.5f : 8.5f));
+        q[j] = min(kMax, max(0, v));
+    }
+    store_u16(dst, f2h(d));
+    if constexpr (kMin) store_u16(dst + 2, f2h(lo));
+    if constexpr (k5) {  // bit e of qh: the fifth bit of element e
+        uint32_t qh = 0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) qh |= (uint32_t)((q[j] >> 4) & 1) << j;
+        store_u16(dst + B::OFF_QH, (uint16_t)qh);
+        store_u16(dst + B::OFF_QH + 2, (uint16_t)(qh >> 16));
+    }
+#pragma unroll
+    for (int j = 0; j < 16; j += 2)  // byte j: element j (low nibble) and element j + 16 (high)
+        store_u16(dst + B::OFF_QS + j, (uint16_t)(((q[j] & 15) | ((q[j + 16] & 15) << 4)) |
+                                                  (((q[j + 1] & 15) | ((q[j + 17] & 15) << 4)) << 8)));
 }
 
 // Block-quantized append without a RoPE: one thread per 32-element block (row (t, b), block
@@ -214,10 +201,13 @@ cudaError_t launch_kv_append(cudaStream_t stream, const cvattn_tensor& c, const 
     if (rows > 0x7fffffffLL) return cudaErrorInvalidValue;
     const unsigned grid = (unsigned)((rows + 7) / 8);
     uint8_t* base = static_cast<uint8_t*>(c.data);
-    // block-quantized caches without a RoPE, f32 rows 16-byte aligned, and enough blocks for at
+    // 4- and 5-bit caches without a RoPE, f32 rows 16-byte aligned, and enough blocks for at
     // least 512 threads per SM: a thread per block.  Smaller launches (the LLM's 256-token
     // prefill calls hold 8,192 blocks) keep a warp per block, which has 32x the threads in flight.
-    const bool block_type = c.type == kQ4_0 || c.type == kQ4_1 || c.type == kQ5_0 || c.type == kQ5_1 || c.type == kQ8_0;
+    // q8_0 keeps the warp form too: a thread's 17 two-byte stores, 34 bytes apart across the warp,
+    // spread each store instruction over ~34 sectors, and that costs more than the warp form's
+    // reductions (DiT step, 1.2 M blocks: 143 us as a thread per block, 94 us as a warp per block).
+    const bool block_type = c.type == kQ4_0 || c.type == kQ4_1 || c.type == kQ5_0 || c.type == kQ5_1;
     const int64_t blocks = rows * groups;
     if (block_type && rp.n_dims == 0 && blocks >= (int64_t)current_sm_count() * kAppendBlockThreadsPerSm &&
         ((reinterpret_cast<uintptr_t>(src) | (uintptr_t)src_nb1 | (uintptr_t)src_nb2) & 15) == 0) {
@@ -233,7 +223,6 @@ cudaError_t launch_kv_append(cudaStream_t stream, const cvattn_tensor& c, const 
             CVATTN_APPEND_BLOCK_CASE(kQ4_1)
             CVATTN_APPEND_BLOCK_CASE(kQ5_0)
             CVATTN_APPEND_BLOCK_CASE(kQ5_1)
-            CVATTN_APPEND_BLOCK_CASE(kQ8_0)
         default: break;
         }
 #undef CVATTN_APPEND_BLOCK_CASE

@@ -70,7 +70,8 @@ def test_append_random_bit_exact(ctx, cv, cuda, oracle, name, heads, batch, n_ne
 @pytest.mark.parametrize("name", ["q8_0", "q5_1", "q5_0", "q4_1", "q4_0"])
 def test_append_dit_launch_bit_exact(ctx, cv, cuda, oracle, name):
     """A DiT-sized append (8 entries x 600 rows of 16 heads x 64: 153,600 blocks) takes the
-    thread-per-block quantizer; its sequential scans must keep ggml's tie rules: the first
+    thread-per-block quantizer for the 4- and 5-bit types (q8_0 keeps the warp form, checked
+    here at the same size); the sequential scans must keep ggml's tie rules: the first
     element of largest magnitude gives q4_0/q5_0 their sign, an all-zero block a zero scale and
     a constant block a zero range.  One position is out of range: that row is skipped and
     reported, the rest are written."""
