@@ -1016,6 +1016,30 @@ def run_profile(args, torch) -> None:
         for _ in range(args.steps):
             cv.kv_append(ctx, kd, k, pos)
             cv.kv_append(ctx, vd, v, pos)
+    elif args.profile == "dit_append_timed":
+        # the same append per cache type, timed (no ncu): CUDA events around 20 back-to-back
+        # launches after 3 warm-ups; TB/s counts the f32 rows read and the cache rows written
+        B, H, P, S = 64, DIT_H, DIT_P, DIT_S
+        src = torch.randn(B, S, H * D, device="cuda")
+        pos = torch.arange(P, P + S, dtype=torch.int32, device="cuda")
+        res = {}
+        for name in ("q8_0", "q4_0", "q5_1", "f16"):
+            t = cv.TYPE_BY_NAME[name]
+            buf, desc = cv.alloc_kv(t, H, D, 1024, B)  # buf holds the cache's memory
+            for _ in range(3):
+                cv.kv_append(ctx, desc, src, pos)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(20):
+                cv.kv_append(ctx, desc, src, pos)
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / 20
+            nbytes = B * S * H * D * 4 + B * S * cv.row_size(t, H * D)
+            res[name] = {"us": round(us, 1), "tbs": round(nbytes / us / 1e6, 2)}
+            del buf, desc
+        print(json.dumps({"dit_append": res}), flush=True)
     else:
         run_flash_secondary(torch, cv, ctx, args, only=args.profile, reps=args.steps)
     torch.cuda.synchronize()
@@ -1032,8 +1056,9 @@ def main() -> None:
     ap.add_argument("--cpu-baselines", action="store_true",
                     help="time the oracle's CPU restatement on bounded samples of every config and print them")
     ap.add_argument("--profile", choices=["decode", "decode_cfg4", "decode_cfg4_q5_1", "dit", "dit_q8_0_q4_0",
-                                          "prefill", "dit_append"], default=None,
-                    help="only launch the named kernel a few times (for an ncu capture); prints nothing")
+                                          "prefill", "dit_append", "dit_append_timed"], default=None,
+                    help="only launch the named kernel a few times (for an ncu capture; prints nothing), "
+                         "or time the DiT append per cache type (dit_append_timed)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
